@@ -1,0 +1,491 @@
+"""Benchmark of the fused Qwen3 decoder-layer memory-bound path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P bench.py --gpus N --steps K --warmup W
+
+Workload: configuration c4 of BASELINE.json -- Qwen3-8B layer shapes (hidden
+4096, 32 q / 8 kv heads, head_dim 128, intermediate 12288), bf16, a mixed
+batch of 32 x 192-token prefill chunks + 2048 decode tokens = 8192 tokens per
+GPU, positions < 32768, a 65536-block (16-token page) KV cache per GPU, seeded
+synthetic inputs with 0.1% x50 outliers.  One step is one pass of the path
+over the batch, in the decoder layer's order:
+
+  embedding gather -> residual add + input RMSNorm -> RoPE cos/sin ->
+  q_norm/k_norm + RoPE + paged KV store -> residual add + post-attn RMSNorm ->
+  SiLU-and-mul
+
+(the GEMMs between them are outside the path; their outputs are seeded
+inputs).  Ranks shard tokens (weak scaling, no collective on the timed path).
+`value` is tokens/s over all ranks, timed with CUDA events (max over ranks);
+`e2e` runs the same step through the public API from pinned host buffers with
+the H2D copies of every per-step input and the D2H copies of every output
+inside the timed region.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "fused-layer tokens/s and HBM GB/s (% of ~8 TB/s) per B200, Qwen3-8B shapes"
+CONFIG = "c4"
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ----------------------------------------------------------------------------
+def hbm_peak() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(kernel: str) -> float | None:
+    """DRAM bytes per launch of `kernel` from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)[kernel]["dram_bytes_per_launch"])
+    except (OSError, KeyError, ValueError, TypeError):
+        return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons with NVML on a background thread."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, device_index: int, interval: float = 0.02):
+        self.samples: list[tuple[int, int]] = []
+        self.interval = interval
+        self._stop = threading.Event()
+        self.ok = False
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self._nvml = None
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                mhz = self._nvml.nvmlDeviceGetClockInfo(self._h, self._nvml.NVML_CLOCK_SM)
+                rs = self._nvml.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((mhz, rs))
+            except Exception:
+                pass
+            time.sleep(self.interval)
+
+    def start(self):
+        if self.ok:
+            self._t.start()
+        return self
+
+    def stop(self) -> dict:
+        self._stop.set()
+        if self.ok:
+            self._t.join(timeout=2)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [],
+                    "samples": 0, "note": "no NVML samples"}
+        busy = [m for m, _ in self.samples]
+        reasons = set()
+        for _, r in self.samples:
+            for bit, name in self.REASONS.items():
+                if r & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(busy), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------
+class Step:
+    """One fused-layer pass over one GPU's batch, through the public API."""
+
+    KERNELS = ["embedding", "add_rmsnorm_in", "rope_cos_sin", "qk_norm_rope_store",
+               "add_rmsnorm_post", "silu_and_mul"]
+
+    def __init__(self, batch):
+        import tinyserver_b200 as tsb
+        from tinyserver_b200 import workloads as W
+
+        self.tsb = tsb
+        self.W = W
+        self.b = batch
+        self.s = batch.cfg.shape
+        self.dt = batch.cfg.dtype
+
+    def run(self, t: dict, events: list | None = None) -> dict:
+        tsb, s = self.tsb, self.s
+        ev = events
+        if ev is not None:
+            ev[0].record()
+        x0 = tsb.embedding(t["input_ids"], t["embed_weight"])
+        if ev is not None:
+            ev[1].record()
+        y1, h1 = tsb.fused_add_rms_norm(t["x_mlp"], x0, t["input_layernorm"], s.eps)
+        if ev is not None:
+            ev[2].record()
+        cos, sin = tsb.rope_cos_sin(t["positions"], t["inv_freq"], s.head_dim, self.dt)
+        if ev is not None:
+            ev[3].record()
+        q, k, v = self.W.qkv_views(t["qkv"], s)
+        q_out, _ = tsb.qk_norm_rope_store(q, k, v, t["q_norm"], t["k_norm"], s.eps, cos, sin,
+                                          t["k_cache"], t["v_cache"], t["block_mapping"],
+                                          t["slot_mapping"], want_k_out=False)
+        if ev is not None:
+            ev[4].record()
+        y2, h2 = tsb.fused_add_rms_norm(t["attn_out"], h1, t["post_attention_layernorm"], s.eps)
+        if ev is not None:
+            ev[5].record()
+        act = tsb.silu_and_mul(t["gate_up"])
+        if ev is not None:
+            ev[6].record()
+        return {"normed_in": y1, "q": q_out, "normed_post": y2, "residual": h2, "act": act}
+
+    def bytes_per_token(self) -> dict[str, int]:
+        bpt = self.W.bytes_per_token(self.s)
+        D = self.s.head_dim
+        elem = torch.tensor([], dtype=self.dt).element_size()
+        return {
+            "embedding": bpt["embedding"],
+            "add_rmsnorm_in": bpt["add_rmsnorm"],
+            "rope_cos_sin": 2 * D * elem + 8,                       # cos+sin rows out, position in
+            "qk_norm_rope_store": bpt["qk_norm_rope_store"] + 2 * D * elem,  # + cos/sin table rows
+            "add_rmsnorm_post": bpt["add_rmsnorm"],
+            "silu_and_mul": bpt["silu_and_mul"],
+        }
+
+
+PER_STEP_INPUTS = ["input_ids", "positions", "block_mapping", "slot_mapping", "x_mlp",
+                   "qkv", "attn_out", "gate_up"]
+
+
+# ----------------------------------------------------------------------------
+def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
+    from tinyserver_b200 import workloads as W
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    batch = W.make_batch(CONFIG, dev, shard=rank)
+    t = batch.tensors
+    T = batch.num_tokens
+    step = Step(batch)
+    bpt = step.bytes_per_token()
+    step_bytes = sum(bpt.values()) * T
+
+    import tinyserver_b200 as tsb
+    tsb.load_library()
+    for _ in range(max(args.warmup, 3)):
+        step.run(t)
+    tsb.check_errors(dev)
+    torch.cuda.synchronize()
+
+    # ---- device-resident timing ---------------------------------------------
+    nk = len(Step.KERNELS)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)]
+           for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local_rank).start()
+    time.sleep(0.05)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    start.record()
+    for i in range(args.steps):
+        step.run(t, evs[i])
+    stop.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = sampler.stop()
+    elapsed_ms = start.elapsed_time(stop)
+    per_kernel_us = {}
+    for j, name in enumerate(Step.KERNELS):
+        per_kernel_us[name] = 1e3 * sum(e[j].elapsed_time(e[j + 1]) for e in evs) / args.steps
+    tsb.check_errors(dev)
+
+    if world > 1:
+        m = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(m, op=torch.distributed.ReduceOp.MAX)
+        elapsed_ms = float(m.item())
+
+    # ---- end to end from pinned host buffers ----------------------------------
+    host_in = {k: t[k].to("cpu").pin_memory() for k in PER_STEP_INPUTS}
+    dev_in = {k: torch.empty_like(t[k]) for k in PER_STEP_INPUTS}
+    resident = {k: v for k, v in t.items() if k not in PER_STEP_INPUTS}
+    outs = step.run(t)
+    host_out = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in outs.items()}
+    h2d = sum(v.numel() * v.element_size() for v in host_in.values())
+    d2h = sum(v.numel() * v.element_size() for v in host_out.values())
+
+    def e2e_step():
+        for k in PER_STEP_INPUTS:
+            dev_in[k].copy_(host_in[k], non_blocking=True)
+        o = step.run({**resident, **dev_in})
+        for k, v in o.items():
+            host_out[k].copy_(v, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 50))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        m = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(m, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(m.item())
+        torch.distributed.barrier()
+
+    if rank != 0:
+        return None
+
+    peak, peak_kind = hbm_peak()
+    ms_per_step = elapsed_ms / args.steps
+    value = world * T * args.steps / (elapsed_ms / 1e3)
+    kernels = {}
+    for name in Step.KERNELS:
+        us = per_kernel_us[name]
+        gbs = bpt[name] * T / (us * 1e-6) / 1e9
+        kernels[name] = {"us": round(us, 2), "bytes_per_token": bpt[name],
+                         "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+    dom = max(Step.KERNELS, key=lambda n: per_kernel_us[n])
+    dom_gbs = bpt[dom] * T / (per_kernel_us[dom] * 1e-6) / 1e9
+    traffic = ncu_traffic(dom)
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: seeded torch.Generator inputs of config c4's shapes and "
+                "distributions (no dataset or checkpoint)",
+        "config": {
+            "workload": "c4: Qwen3-8B layer, mixed 32x192 prefill + 2048 decode = "
+                        "8192 tokens/GPU, 16-token pages, 65536 blocks/GPU",
+            "tokens_per_gpu": T, "global_tokens": world * T, "hidden": 4096,
+            "num_q_heads": 32, "num_kv_heads": 8, "head_dim": 128, "intermediate": 12288,
+            "parallelism": f"token-sharded x{world}, no collective on the timed path",
+            "l2": f"inputs larger than L2: {step_bytes / 1e9:.2f} GB moved per step per GPU",
+        },
+        "hbm_gbs": round(step_bytes / (ms_per_step * 1e-3) / 1e9, 1),
+        "hbm_frac": round(step_bytes / (ms_per_step * 1e-3) / 1e9 / peak, 4),
+        "hbm_peak_gbs": peak,
+        "hbm_peak_kind": peak_kind,
+        "kernels": kernels,
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(dom_gbs, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(dom_gbs / peak, 4),
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                     if peak_kind == "measured" else "fallback 6650 GB/s",
+                     "algorithmic_bytes_per_launch": bpt[dom] * T,
+                     "traffic": traffic},
+        "gpu_launches": nk * args.steps,
+        "clocks": clocks,
+        "e2e": {"value": round(world * T * e2e_steps / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "steps": e2e_steps,
+                "note": "public API from pinned host buffers; every per-step input H2D and "
+                        "every output D2H inside the timed region (single stream)"},
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(batch, budget_s=args.cpu_seconds)
+    return line
+
+
+# ----------------------------------------------------------------------------
+def _reference_inputs(batch, n_tokens: int, device="cpu"):
+    """The first n_tokens of the batch (CPU copies) for the reference CPU path."""
+    t = batch.tensors
+    sl = slice(0, n_tokens)
+    keys = ["input_ids", "positions", "x_mlp", "residual", "qkv", "attn_out", "gate_up",
+            "block_mapping", "slot_mapping"]
+    out = {k: t[k][sl].to(device) for k in keys}
+    return out
+
+
+def cpu_baseline(batch, budget_s: float = 10.0, threads: int | None = None,
+                 max_tokens: int = 512) -> dict:
+    """Time the reference's CPU path (transformers modules + index_put store) on
+    a bounded sample of the batch; returns tokens/s over that sample."""
+    from oracle.ref_torch_cpu import ReferenceLayerPath
+
+    threads = threads or os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    t = batch.tensors
+    s = batch.cfg.shape
+    weights = {"embed_weight": t["embed_weight"].to("cpu")}
+    for k in ("input_layernorm", "post_attention_layernorm", "q_norm", "k_norm"):
+        weights[k] = t[k].to("cpu")
+    ref = ReferenceLayerPath(s, batch.cfg.dtype, weights)
+    # a CPU cache large enough for the sample's slots (same page geometry)
+    n = min(max_tokens, batch.num_tokens)
+    inp = _reference_inputs(batch, n)
+    bm = inp.pop("block_mapping")
+    sm = inp.pop("slot_mapping")
+    uniq, bm_local = torch.unique(bm, return_inverse=True)
+    kc = torch.zeros(len(uniq), s.num_kv_heads, batch.cfg.block_size, s.head_dim,
+                     dtype=batch.cfg.dtype)
+    vc = torch.zeros_like(kc)
+
+    def once():
+        ref.step(inp["input_ids"], inp["positions"], inp["x_mlp"], inp["residual"], inp["qkv"],
+                 inp["attn_out"], inp["gate_up"], kc, vc, bm_local, sm)
+
+    once()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        once()
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": round(n / med, 1), "unit": "tokens/s", "cores": threads,
+            "kind": "reference",
+            "sample": f"{n} tokens of c4 per step, median of {len(times)} steps "
+                      f"({sum(times):.1f} s); transformers {__import__('transformers').__version__}"
+                      " Qwen3 modules + torch index_put KV store, bf16, "
+                      f"torch.set_num_threads({threads})"}
+
+
+def run_reference(args, rank: int) -> dict | None:
+    """--impl reference: the reference's torch CPU path on the host cores."""
+    if rank != 0:
+        return None
+    from tinyserver_b200 import workloads as W
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    batch = W.make_batch(CONFIG, "cpu", poison_cache=False)
+    from oracle.ref_torch_cpu import ReferenceLayerPath
+
+    t = batch.tensors
+    s = batch.cfg.shape
+    weights = {k: t[k] for k in ("embed_weight", "input_layernorm", "post_attention_layernorm",
+                                 "q_norm", "k_norm")}
+    ref = ReferenceLayerPath(s, batch.cfg.dtype, weights)
+
+    def make(n):
+        inp = _reference_inputs(batch, n)
+        bm = inp.pop("block_mapping")
+        sm = inp.pop("slot_mapping")
+        uniq, bm_local = torch.unique(bm, return_inverse=True)
+        kc = torch.zeros(len(uniq), s.num_kv_heads, batch.cfg.block_size, s.head_dim,
+                         dtype=batch.cfg.dtype)
+        return inp, kc, torch.zeros_like(kc), bm_local, sm
+
+    def run(pack):
+        inp, kc, vc, bm, sm = pack
+        ref.step(inp["input_ids"], inp["positions"], inp["x_mlp"], inp["residual"], inp["qkv"],
+                 inp["attn_out"], inp["gate_up"], kc, vc, bm, sm)
+
+    # size the per-step sample so the whole run stays near args.cpu_total seconds
+    probe = make(64)
+    run(probe)
+    t0 = time.perf_counter()
+    run(probe)
+    per_tok = (time.perf_counter() - t0) / 64
+    budget = args.cpu_total / max(1, args.steps + args.warmup)
+    n = int(max(16, min(batch.num_tokens, budget / per_tok)))
+    pack = make(n)
+    for _ in range(args.warmup):
+        run(pack)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        run(pack)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = n * args.steps / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded torch.Generator inputs of config c4",
+        "config": {"workload": "c4: Qwen3-8B layer, mixed prefill+decode batch; each step a "
+                               f"{n}-token sample of the 8192-token batch",
+                   "tokens_per_step": n},
+        "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": threads,
+                         "kind": "reference",
+                         "sample": f"{n} tokens of c4 per step on the host CPU: transformers "
+                                   "Qwen3 modules + torch index_put KV store (the reference's "
+                                   "Triton store has no CPU path)"},
+        "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    return line
+
+
+# ----------------------------------------------------------------------------
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU-baseline timing budget (ours arm)")
+    ap.add_argument("--cpu-total", type=float, default=90.0,
+                    help="total CPU time budget of the --impl reference run")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        line = run_reference(args, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

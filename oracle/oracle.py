@@ -1,0 +1,236 @@
+"""ctypes front end of the C oracle (``qwen3_oracle.c``).
+
+TEST INFRASTRUCTURE ONLY: the parity checker for tinyserver_b200's CUDA path.
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
+leg may import this module.  The product never does.
+
+Every function takes and returns CPU torch tensors and mirrors one op of the
+reference path (citations are in the C source):
+
+* :func:`embedding`       -- ``nn.Embedding`` gather (HF:363, HF:392)
+* :func:`rmsnorm`         -- ``Qwen3RMSNorm.forward`` (HF:59-64)
+* :func:`add_rmsnorm`     -- residual add (HF:327/333) + ``Qwen3RMSNorm``
+* :func:`rope_cos_sin`    -- ``Qwen3RotaryEmbedding.forward`` (HF:137-148)
+* :func:`qk_norm_rope_store` -- q_norm/k_norm + ``apply_rotary_pos_emb`` + paged
+  store, as ``server/model/patches/qwen3.py:264-318`` runs them
+* :func:`kv_store_batched` / :func:`kv_store_seq` -- ``server/model/kernels/
+  kv_cache.py`` ``store_kv_cache_batched`` / ``store_kv_cache``
+* :func:`silu_and_mul`    -- ``Qwen3MLP`` activation product (HF:81-83)
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "lib", "liboracle_qwen3.so")
+_lib = None
+
+DTYPE_TAG = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+c_i64 = ctypes.c_int64
+c_vp = ctypes.c_void_p
+c_int = ctypes.c_int
+c_float = ctypes.c_float
+I64x = ctypes.POINTER(ctypes.c_int64)
+
+
+def build() -> str:
+    """Compile the oracle with the committed Makefile; return the library path."""
+    src = os.path.join(_HERE, "qwen3_oracle.c")
+    if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+        subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        _lib = ctypes.CDLL(build())
+        sig = {
+            "oracle_embedding": [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_int, c_vp, c_i64],
+            "oracle_rmsnorm": [c_vp, c_i64, c_vp, c_i64, c_i64, c_float, c_int, c_vp, c_i64],
+            "oracle_add_rmsnorm": [c_vp, c_vp, c_vp, c_i64, c_i64, c_float, c_int, c_vp, c_vp],
+            "oracle_rope_cos_sin": [c_vp, c_i64, c_vp, c_i64, c_float, c_int, c_vp, c_vp],
+            "oracle_qk_norm_rope_store": [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64,
+                                          c_i64, c_vp, c_vp, c_float, c_vp, c_vp, c_i64, c_i64,
+                                          c_i64, c_i64, c_i64, c_int, c_vp, c_vp, c_vp, c_vp,
+                                          I64x, c_i64, c_i64, c_vp, c_vp, c_int],
+            "oracle_kv_store_batched": [c_vp, I64x, c_vp, I64x, c_vp, c_vp, I64x, c_vp, c_vp,
+                                        c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_int],
+            "oracle_kv_store_seq": [c_i64, c_vp, c_i64, c_int, c_vp, I64x, c_vp, I64x, c_vp,
+                                    c_vp, I64x, c_i64, c_i64, c_i64, c_i64, c_i64, c_int],
+            "oracle_silu_and_mul": [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_int, c_vp, c_i64],
+            "oracle_num_threads": [],
+        }
+        for name, argtypes in sig.items():
+            fn = getattr(_lib, name)
+            fn.argtypes = argtypes
+            fn.restype = c_int
+    return _lib
+
+
+def num_threads() -> int:
+    return lib().oracle_num_threads()
+
+
+def _p(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _arr(vals) -> ctypes.Array:
+    return (ctypes.c_int64 * len(vals))(*[int(v) for v in vals])
+
+
+def _cpu(t: torch.Tensor) -> torch.Tensor:
+    if t.device.type != "cpu":
+        raise ValueError("oracle takes CPU tensors")
+    return t
+
+
+def _check(rc: int, what: str) -> None:
+    if rc == 2:
+        raise IndexError(f"oracle {what}: index out of range")
+    if rc != 0:
+        raise ValueError(f"oracle {what}: bad argument (rc={rc})")
+
+
+def embedding(ids: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
+    ids = _cpu(ids).reshape(-1).to(torch.int64).contiguous()
+    table = _cpu(table)
+    assert table.stride(1) == 1
+    V, H = table.shape
+    out = torch.empty(ids.numel(), H, dtype=table.dtype)
+    _check(lib().oracle_embedding(_p(ids), ids.numel(), _p(table), V, H, table.stride(0),
+                                  DTYPE_TAG[table.dtype], _p(out), H), "embedding")
+    return out
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    x = _cpu(x).contiguous()
+    H = x.shape[-1]
+    x2 = x.reshape(-1, H)
+    w = w.to(x.dtype).contiguous()
+    out = torch.empty_like(x2)
+    _check(lib().oracle_rmsnorm(_p(x2), H, _p(w), x2.shape[0], H, eps, DTYPE_TAG[x.dtype],
+                                _p(out), H), "rmsnorm")
+    return out.reshape(x.shape)
+
+
+def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
+                eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """Return (normed, new_residual) where new_residual = residual + x."""
+    x = _cpu(x).contiguous()
+    residual = _cpu(residual).contiguous()
+    H = x.shape[-1]
+    T = x.numel() // H
+    w = w.to(x.dtype).contiguous()
+    h = torch.empty_like(x)
+    y = torch.empty_like(x)
+    _check(lib().oracle_add_rmsnorm(_p(x), _p(residual), _p(w), T, H, eps, DTYPE_TAG[x.dtype],
+                                    _p(h), _p(y)), "add_rmsnorm")
+    return y, h
+
+
+def rope_inv_freq(head_dim: int, theta: float) -> torch.Tensor:
+    """inv_freq exactly as compute_default_rope_parameters builds it (HF:125-132)."""
+    return 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).to(dtype=torch.float)
+                            / head_dim))
+
+
+def rope_cos_sin(positions: torch.Tensor, inv_freq: torch.Tensor, head_dim: int,
+                 dtype: torch.dtype, scaling: float = 1.0) -> tuple[torch.Tensor, torch.Tensor]:
+    pos = _cpu(positions).reshape(-1).to(torch.int64).contiguous()
+    inv = _cpu(inv_freq).to(torch.float32).contiguous()
+    T = pos.numel()
+    cos = torch.empty(T, head_dim, dtype=dtype)
+    sin = torch.empty(T, head_dim, dtype=dtype)
+    _check(lib().oracle_rope_cos_sin(_p(pos), T, _p(inv), head_dim, scaling, DTYPE_TAG[dtype],
+                                     _p(cos), _p(sin)), "rope_cos_sin")
+    return cos, sin
+
+
+def qk_norm_rope_store(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor | None,
+                       q_w: torch.Tensor | None, k_w: torch.Tensor | None, eps: float,
+                       cos: torch.Tensor, sin: torch.Tensor,
+                       k_cache: torch.Tensor | None = None, v_cache: torch.Tensor | None = None,
+                       block_mapping: torch.Tensor | None = None,
+                       slot_mapping: torch.Tensor | None = None,
+                       want_k_out: bool = True):
+    """q: (T, Hq, D), k/v: (T, Hkv, D) (last dim contiguous), cos/sin: (T, D).
+
+    Returns (q_out (T,Hq,D), k_out (T,Hkv,D) or None); mutates the caches.
+    """
+    T, Hq, D = q.shape
+    Hkv = k.shape[1]
+    dt = q.dtype
+    for t in (q, k) + ((v,) if v is not None else ()):
+        _cpu(t)
+        assert t.stride(2) == 1 and t.dtype == dt
+    cos = cos.reshape(T, D).contiguous()
+    sin = sin.reshape(T, D).contiguous()
+    q_out = torch.empty(T, Hq, D, dtype=dt)
+    k_out = torch.empty(T, Hkv, D, dtype=dt) if want_k_out else None
+    qw = q_w.to(dt).contiguous() if q_w is not None else None
+    kw = k_w.to(dt).contiguous() if k_w is not None else None
+    if k_cache is not None:
+        bm = block_mapping.contiguous()
+        sm = slot_mapping.to(bm.dtype).contiguous()
+        idx64 = int(bm.dtype == torch.int64)
+        c = _arr(k_cache.stride())
+        N, B = k_cache.shape[0], k_cache.shape[2]
+        assert k_cache.stride() == v_cache.stride()
+    else:
+        bm = sm = None
+        idx64 = 1
+        c = _arr([0, 0, 0, 0])
+        N = B = 0
+    vv = v if v is not None else None
+    _check(lib().oracle_qk_norm_rope_store(
+        _p(q), q.stride(0), q.stride(1), _p(k), k.stride(0), k.stride(1),
+        _p(vv), vv.stride(0) if vv is not None else 0, vv.stride(1) if vv is not None else 0,
+        _p(qw), _p(kw), eps, _p(cos), _p(sin), D, T, Hq, Hkv, D, DTYPE_TAG[dt],
+        _p(q_out), _p(k_out), _p(k_cache), _p(v_cache), c, N, B, _p(bm), _p(sm), idx64),
+        "qk_norm_rope_store")
+    return q_out, k_out
+
+
+def kv_store_batched(k_src: torch.Tensor, v_src: torch.Tensor, k_cache: torch.Tensor,
+                     v_cache: torch.Tensor, block_mapping: torch.Tensor,
+                     slot_mapping: torch.Tensor) -> None:
+    Hkv, T, D = k_src.shape
+    assert k_cache.stride() == v_cache.stride()
+    bm = _cpu(block_mapping).contiguous()
+    sm = _cpu(slot_mapping).to(bm.dtype).contiguous()
+    _check(lib().oracle_kv_store_batched(
+        _p(k_src), _arr(k_src.stride()), _p(v_src), _arr(v_src.stride()), _p(k_cache),
+        _p(v_cache), _arr(k_cache.stride()), _p(bm), _p(sm), int(bm.dtype == torch.int64),
+        T, Hkv, D, k_cache.shape[0], k_cache.shape[2], k_src.element_size()),
+        "kv_store_batched")
+
+
+def kv_store_seq(start_position: int, block_table: torch.Tensor, k_src: torch.Tensor,
+                 v_src: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor) -> None:
+    Hkv, T, D = k_src.shape
+    bt = _cpu(block_table).contiguous()
+    _check(lib().oracle_kv_store_seq(
+        int(start_position), _p(bt), bt.numel(), int(bt.dtype == torch.int64), _p(k_src),
+        _arr(k_src.stride()), _p(v_src), _arr(v_src.stride()), _p(k_cache), _p(v_cache),
+        _arr(k_cache.stride()), T, Hkv, D, k_cache.shape[0], k_cache.shape[2],
+        k_src.element_size()), "kv_store_seq")
+
+
+def silu_and_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """gate, up: (T, I) views (row strides free, last dim contiguous)."""
+    _cpu(gate)
+    _cpu(up)
+    T, I = gate.shape
+    assert gate.stride(1) == 1 and up.stride(1) == 1 and gate.dtype == up.dtype
+    out = torch.empty(T, I, dtype=gate.dtype)
+    _check(lib().oracle_silu_and_mul(_p(gate), gate.stride(0), _p(up), up.stride(0), T, I,
+                                     DTYPE_TAG[gate.dtype], _p(out), I), "silu_and_mul")
+    return out

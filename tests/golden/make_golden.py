@@ -1,0 +1,338 @@
+"""Generate the golden fixtures in tests/golden/ from the reference's own code.
+
+Run in a container that has the reference checkout (default path below, or
+``TINYSERVER_REF``); the GPU box never runs this script, it only reads the
+fixtures it wrote::
+
+    python tests/golden/make_golden.py [--ref /path/to/tinyserver]
+
+What produces the golden outputs:
+
+* ``layer_{bf16,f32}.pt`` -- one forward of a 1-layer random-init Qwen3 model
+  (transformers 5.5.0) patched by the reference's ``qwen3_model_patcher``
+  (server/model/patches/qwen3.py:469-479), for a prefill batch and then a
+  decode step, exactly as the reference's test helpers drive it
+  (tests/model/paged_helpers.py:37-77).  Forward hooks capture every
+  memory-bound op on the hot path: the embedding gather, input/post-attention
+  RMSNorm with the residual add, q_norm/k_norm, the output of
+  ``apply_rotary_pos_emb`` (wrapped where qwen3.py imports it), the paged KV
+  cache before/after the reference's Triton store kernels, and the SiLU-and-mul
+  product that feeds down_proj.  The Triton kernels run on CPU through Triton's
+  interpreter (TRITON_INTERPRET=1).
+* ``kv_store.pt`` -- the reference's two store kernels
+  (server/model/kernels/kv_cache.py) on the scenarios of the reference's own
+  tests (tests/model/test_kv_cache_kernels.py:73-207) plus a bf16, head_dim 128
+  case with a permuted block table, int64 mappings and a poisoned cache.
+* ``rope_cos_sin.pt`` -- Qwen3RotaryEmbedding (theta 1e6, head_dim 128) at
+  positions up to 131071 in fp32 and bf16.
+* ``outliers.pt`` -- Qwen3RMSNorm with the decoder layer's residual add at
+  hidden 4096 with x50 outliers, and ACT2FN["silu"](gate) * up on
+  large-magnitude inputs, in bf16.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+os.environ.setdefault("TRITON_INTERPRET", "1")
+
+import torch  # noqa: E402
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _seeded_(module: torch.nn.Module, gen: torch.Generator) -> None:
+    """Overwrite every parameter with seeded values: N(0, 0.02) for matrices,
+    1 + N(0, 0.02) for norm weights (vectors)."""
+    with torch.no_grad():
+        for name, p in module.named_parameters():
+            noise = torch.randn(p.shape, generator=gen, dtype=torch.float32) * 0.02
+            if p.dim() == 1:
+                p.copy_(1.0 + noise)
+            else:
+                p.copy_(noise)
+
+
+def _layer_case(dtype: torch.dtype, seq_lens: list[int], seed: int, vocab: int,
+                num_blocks: int) -> dict:
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    import server.model.patches.qwen3 as refq
+    from server.model.inference_context import InferenceContext, inference_context
+    from server.model.prefill_helpers import build_prefill_inputs
+
+    gen = torch.Generator().manual_seed(seed)
+    cfg = Qwen3Config(
+        vocab_size=vocab, hidden_size=1024, intermediate_size=1024, num_hidden_layers=1,
+        num_attention_heads=16, num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-6,
+        rope_parameters={"rope_type": "default", "rope_theta": 1e6},
+        max_position_embeddings=40960, tie_word_embeddings=False,
+    )
+    model = Qwen3ForCausalLM(cfg).eval()
+    _seeded_(model, gen)
+    model = model.to(dtype)
+    layer = model.model.layers[0]
+    attn = layer.self_attn
+
+    block_size = 16
+    pool = torch.randn(2, 1, num_blocks, 8, block_size, 128, generator=gen).to(dtype)
+    refq.qwen3_model_patcher(model)
+    attn.k_cache = pool[0, 0]
+    attn.v_cache = pool[1, 0]
+
+    cap: dict[str, list] = {}
+
+    def hook(name):
+        def fn(_mod, args, out):
+            cap.setdefault(name + ".in", []).append(args[0].detach().clone())
+            o = out[0] if isinstance(out, tuple) else out
+            cap.setdefault(name + ".out", []).append(o.detach().clone())
+        return fn
+
+    model.model.embed_tokens.register_forward_hook(hook("embed"))
+    layer.input_layernorm.register_forward_hook(hook("input_layernorm"))
+    layer.post_attention_layernorm.register_forward_hook(hook("post_attention_layernorm"))
+    attn.q_proj.register_forward_hook(hook("q_proj"))
+    attn.k_proj.register_forward_hook(hook("k_proj"))
+    attn.v_proj.register_forward_hook(hook("v_proj"))
+    attn.q_norm.register_forward_hook(hook("q_norm"))
+    attn.k_norm.register_forward_hook(hook("k_norm"))
+    attn.o_proj.register_forward_hook(hook("o_proj"))
+    layer.mlp.gate_proj.register_forward_hook(hook("gate_proj"))
+    layer.mlp.up_proj.register_forward_hook(hook("up_proj"))
+    layer.mlp.down_proj.register_forward_hook(hook("down_proj"))
+    # inputs that repeat another capture (every projection reads the normed
+    # hidden state; q/k_norm read the projections; rope reads q/k_norm's output)
+    redundant = {"q_proj.in", "k_proj.in", "v_proj.in", "gate_proj.in", "up_proj.in",
+                 "q_norm.in", "k_norm.in", "o_proj.in", "post_attention_layernorm.out.dup"}
+
+    orig_rope = refq.apply_rotary_pos_emb
+
+    def rope_wrap(q, k, cos, sin, *a, **kw):
+        qo, ko = orig_rope(q, k, cos, sin, *a, **kw)
+        cap.setdefault("rope.cos", []).append(cos.detach().clone())
+        cap.setdefault("rope.sin", []).append(sin.detach().clone())
+        cap.setdefault("rope.q_out", []).append(qo.detach().clone())
+        cap.setdefault("rope.k_out", []).append(ko.detach().clone())
+        return qo, ko
+
+    refq.apply_rotary_pos_emb = rope_wrap
+
+    perm = torch.randperm(num_blocks, generator=gen).tolist()
+    # capacity for prompt + one decode token per sequence
+    need = [-(-(n + 1) // block_size) for n in seq_lens]
+    block_tables, cur = [], 0
+    for n in need:
+        block_tables.append(perm[cur:cur + n])
+        cur += n
+    assert cur <= num_blocks
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=gen).tolist() for n in seq_lens]
+
+    cache_before = pool.clone()
+    written_prefill = [(bt[j // block_size], j % block_size)
+                       for n, bt in zip(seq_lens, block_tables) for j in range(n)]
+    written_decode = [(bt[n // block_size], n % block_size)
+                      for n, bt in zip(seq_lens, block_tables)]
+    input_ids, position_ids, ctx = build_prefill_inputs(prompts, block_tables, "cpu")
+    try:
+        with torch.no_grad(), inference_context(ctx):
+            model(input_ids=input_ids, position_ids=position_ids, use_cache=False)
+        cache_after_prefill = pool.clone()
+        next_tokens = torch.randint(0, cfg.vocab_size, (len(seq_lens),), generator=gen).tolist()
+        dec_ids = torch.tensor([next_tokens], dtype=torch.long)
+        dec_pos = torch.tensor([seq_lens], dtype=torch.long)
+        dctx = InferenceContext(mode="decode", sequences=[
+            {"num_tokens": 1, "block_table": bt} for bt in block_tables])
+        with torch.no_grad(), inference_context(dctx):
+            model(input_ids=dec_ids, position_ids=dec_pos, use_cache=False)
+        cache_after_decode = pool.clone()
+    finally:
+        refq.apply_rotary_pos_emb = orig_rope
+
+    out = {
+        "dtype": str(dtype), "hidden": 1024, "num_q_heads": 16, "num_kv_heads": 8,
+        "head_dim": 128, "intermediate": 1024, "eps": 1e-6, "rope_theta": 1e6,
+        "block_size": block_size, "num_blocks": num_blocks, "seq_lens": seq_lens,
+        "block_tables": block_tables, "prefill_input_ids": input_ids.clone(),
+        "prefill_position_ids": position_ids.clone(), "decode_input_ids": dec_ids,
+        "decode_position_ids": dec_pos, "embed_weight": model.model.embed_tokens.weight.detach().clone(),
+        "input_layernorm_weight": layer.input_layernorm.weight.detach().clone(),
+        "post_attention_layernorm_weight": layer.post_attention_layernorm.weight.detach().clone(),
+        "q_norm_weight": attn.q_norm.weight.detach().clone(),
+        "k_norm_weight": attn.k_norm.weight.detach().clone(),
+        "inv_freq": model.model.rotary_emb.inv_freq.detach().clone(),
+        "cache_before": cache_before,
+        "written_prefill": written_prefill, "written_decode": written_decode,
+        "rows_after_prefill": _written_rows(cache_before, cache_after_prefill, written_prefill),
+        "rows_after_decode": _written_rows(cache_after_prefill, cache_after_decode,
+                                           written_decode),
+    }
+    for key, vals in cap.items():
+        if key in redundant:
+            continue
+        assert len(vals) == 2, (key, len(vals))  # [prefill, decode]
+        out[key] = vals
+    return out
+
+
+def _written_rows(before: torch.Tensor, after: torch.Tensor, written: list) -> torch.Tensor:
+    """Rows (2, len(written), Hkv, D) of the (K, V) pool at the written (block, slot)
+    pairs, after checking that no other cache row changed.  before/after are
+    pools of shape (2, 1, N, Hkv, B, D)."""
+    changed = after.ne(before).any(dim=-1)  # (2, 1, N, Hkv, B)
+    expect = torch.zeros_like(changed)
+    for b, s in written:
+        expect[:, :, b, :, s] = True
+    assert not (changed & ~expect).any(), "reference wrote outside the mapped slots"
+    idx_b = torch.tensor([b for b, _ in written])
+    idx_s = torch.tensor([s for _, s in written])
+    return after[:, 0, idx_b, :, idx_s, :].clone()
+
+
+def _kv_store_case() -> dict:
+    from server.model.kernels.kv_cache import store_kv_cache, store_kv_cache_batched
+
+    gen = torch.Generator().manual_seed(4321)
+    cases = []
+    # The scenarios of tests/model/test_kv_cache_kernels.py:73-207 (fp32).
+    scen = [
+        ("single_seq", 2, 4, 8, 2, [{"start_pos": 0, "seq_len": 4, "block_table": [0]}]),
+        ("multiple_seqs", 4, 4, 16, 4, [
+            {"start_pos": 0, "seq_len": 3, "block_table": [0]},
+            {"start_pos": 0, "seq_len": 5, "block_table": [1, 2]},
+            {"start_pos": 0, "seq_len": 4, "block_table": [3]}]),
+        ("multi_block", 2, 4, 32, 3, [{"start_pos": 0, "seq_len": 12, "block_table": [0, 1, 2]}]),
+        ("single_token", 2, 4, 8, 3, [
+            {"start_pos": 0, "seq_len": 1, "block_table": [0]},
+            {"start_pos": 0, "seq_len": 1, "block_table": [1]},
+            {"start_pos": 0, "seq_len": 1, "block_table": [2]}]),
+        ("nonzero_start", 2, 4, 8, 3, [
+            {"start_pos": 4, "seq_len": 3, "block_table": [0, 1]},
+            {"start_pos": 8, "seq_len": 4, "block_table": [0, 0, 2]}]),
+    ]
+    for name, hkv, bsz, hd, nblk, seqs in scen:
+        cases.append(_store_one(name, torch.float32, hkv, bsz, hd, nblk, seqs, torch.int32, gen,
+                                store_kv_cache, store_kv_cache_batched, poison=False))
+    # bf16, Qwen3 head geometry, permuted blocks, int64 mappings, poisoned cache.
+    perm = torch.randperm(16, generator=gen).tolist()
+    seqs = [
+        {"start_pos": 0, "seq_len": 37, "block_table": perm[0:3]},
+        {"start_pos": 21, "seq_len": 20, "block_table": perm[3:6]},
+        {"start_pos": 0, "seq_len": 1, "block_table": perm[6:7]},
+        {"start_pos": 95, "seq_len": 1, "block_table": perm[7:14]},
+    ]
+    cases.append(_store_one("bf16_permuted", torch.bfloat16, 8, 16, 128, 16, seqs, torch.int64,
+                            gen, store_kv_cache, store_kv_cache_batched, poison=True))
+    return {"cases": cases}
+
+
+def _store_one(name, dtype, hkv, bsz, hd, nblk, seqs, idx_dtype, gen, per_seq, batched, poison):
+    k_srcs = [torch.randn(hkv, s["seq_len"], hd, generator=gen).to(dtype) for s in seqs]
+    v_srcs = [torch.randn(hkv, s["seq_len"], hd, generator=gen).to(dtype) for s in seqs]
+    shape = (nblk, hkv, bsz, hd)
+    if poison:
+        base_k = torch.randn(shape, generator=gen).to(dtype)
+        base_v = torch.randn(shape, generator=gen).to(dtype)
+    else:
+        base_k = torch.zeros(shape, dtype=dtype)
+        base_v = torch.zeros(shape, dtype=dtype)
+    # per-sequence kernel (kv_cache.py:6-119)
+    k_ref, v_ref = base_k.clone(), base_v.clone()
+    for s, ks, vs in zip(seqs, k_srcs, v_srcs):
+        per_seq(s["start_pos"], torch.tensor(s["block_table"], dtype=torch.int32), ks, vs,
+                k_ref, v_ref)
+    # batched kernel (kv_cache.py:122-251) with the reference tests' mapping recipe
+    # (tests/model/test_kv_cache_kernels.py:16-37)
+    bm, sm = [], []
+    for s in seqs:
+        for i in range(s["seq_len"]):
+            p = s["start_pos"] + i
+            bm.append(s["block_table"][p // bsz])
+            sm.append(p % bsz)
+    bm_t = torch.tensor(bm, dtype=idx_dtype)
+    sm_t = torch.tensor(sm, dtype=idx_dtype)
+    k_bat, v_bat = base_k.clone(), base_v.clone()
+    batched(torch.cat(k_srcs, 1), torch.cat(v_srcs, 1), k_bat, v_bat, bm_t, sm_t)
+    assert torch.equal(k_bat, k_ref) and torch.equal(v_bat, v_ref), name
+    assert len(set(zip(bm, sm))) == len(bm), "golden mappings must not collide"
+    pool_before = torch.stack([base_k, base_v])[:, None]
+    pool_after = torch.stack([k_bat, v_bat])[:, None]
+    return {"name": name, "seqs": seqs, "k_srcs": k_srcs, "v_srcs": v_srcs,
+            "cache_k_before": base_k, "cache_v_before": base_v,
+            "block_mapping": bm_t, "slot_mapping": sm_t,
+            "written_rows": _written_rows(pool_before, pool_after, list(zip(bm, sm)))}
+
+
+def _rope_case() -> dict:
+    from transformers import Qwen3Config
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RotaryEmbedding
+
+    cfg = Qwen3Config(hidden_size=1024, num_attention_heads=16, num_key_value_heads=8,
+                      head_dim=128, rope_parameters={"rope_type": "default", "rope_theta": 1e6},
+                      max_position_embeddings=131072)
+    rot = Qwen3RotaryEmbedding(cfg)
+    gen = torch.Generator().manual_seed(77)
+    pos = torch.cat([torch.arange(0, 64), torch.randint(0, 131072, (192,), generator=gen),
+                     torch.tensor([8191, 16383, 32767, 65535, 131071])]).to(torch.int64)[None]
+    out = {"positions": pos, "inv_freq": rot.inv_freq.clone(), "head_dim": 128,
+           "rope_theta": 1e6}
+    for dt in (torch.float32, torch.bfloat16):
+        cos, sin = rot(torch.zeros(1, dtype=dt), pos)
+        out[f"cos_{dt}"] = cos[0]
+        out[f"sin_{dt}"] = sin[0]
+    return out
+
+
+def _outlier_case() -> dict:
+    from transformers.activations import ACT2FN
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm
+
+    gen = torch.Generator().manual_seed(99)
+    H, T = 4096, 24
+    x = torch.randn(T, H, generator=gen)
+    mask = torch.rand(T, H, generator=gen) < 0.001
+    x = torch.where(mask, x * 50.0, x).to(torch.bfloat16)
+    res = torch.randn(T, H, generator=gen).mul(0.5).to(torch.bfloat16)
+    norm = Qwen3RMSNorm(H, eps=1e-6)
+    with torch.no_grad():
+        norm.weight.copy_(1.0 + 0.02 * torch.randn(H, generator=gen))
+    norm = norm.to(torch.bfloat16)
+    with torch.no_grad():
+        h = res + x  # Qwen3DecoderLayer residual add (HF:327)
+        y = norm(h)
+    I = 2048
+    gate = (torch.randn(T, I, generator=gen) * 6.0).to(torch.bfloat16)
+    gate[0, :8] = torch.tensor([-100., -50., -20., -1e-3, 0., 1e-3, 20., 90.])
+    up = torch.randn(T, I, generator=gen).to(torch.bfloat16)
+    with torch.no_grad():
+        act = ACT2FN["silu"](gate) * up  # Qwen3MLP (HF:82)
+    return {"x": x, "residual": res, "weight": norm.weight.detach().clone(), "eps": 1e-6,
+            "h": h, "y": y, "gate": gate, "up": up, "act": act}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default=os.environ.get("TINYSERVER_REF", "/root/reference"))
+    args = ap.parse_args()
+    sys.path.insert(0, args.ref)
+    import transformers
+    torch.manual_seed(0)
+    meta = {"transformers": transformers.__version__, "torch": torch.__version__}
+    for dt, lens, seed, vocab, nblk, fname in (
+            (torch.bfloat16, [5, 16, 37], 1234, 128, 8, "layer_bf16.pt"),
+            (torch.float32, [3, 17], 1235, 128, 4, "layer_f32.pt")):
+        d = _layer_case(dt, lens, seed, vocab, nblk)
+        d["meta"] = meta
+        torch.save(d, os.path.join(HERE, fname))
+    torch.save({**_kv_store_case(), "meta": meta}, os.path.join(HERE, "kv_store.pt"))
+    torch.save({**_rope_case(), "meta": meta}, os.path.join(HERE, "rope_cos_sin.pt"))
+    torch.save({**_outlier_case(), "meta": meta}, os.path.join(HERE, "outliers.pt"))
+    for f in sorted(os.listdir(HERE)):
+        if f.endswith(".pt"):
+            print(f, os.path.getsize(os.path.join(HERE, f)))
+
+
+if __name__ == "__main__":
+    main()

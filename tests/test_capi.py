@@ -1,0 +1,83 @@
+"""The C-ABI library on a machine without a GPU: it builds, loads, exports
+every entry point include/qwen3fused.h declares, agrees with the Python
+binding on the argument struct, and rejects bad arguments on the host before
+touching the device."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from tinyserver_b200 import _capi
+
+HEADER_DIR = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+
+
+def declared_functions() -> set[str]:
+    names = set()
+    for f in os.listdir(HEADER_DIR):
+        if not f.endswith(".h"):
+            continue
+        text = open(os.path.join(HEADER_DIR, f)).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names |= set(re.findall(r"^[A-Za-z_][\w\s\*]*?\b(qf_\w+)\s*\(", text, flags=re.M))
+    return names
+
+
+def test_header_declares_the_expected_entry_points():
+    names = declared_functions()
+    for required in ("qf_kv_store_batched", "qf_kv_store_seq", "qf_rmsnorm", "qf_add_rmsnorm",
+                     "qf_rope_cos_sin", "qf_qk_norm_rope_store", "qf_silu_and_mul",
+                     "qf_embedding", "qf_build_slot_mapping", "qf_read_status"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _capi.lib()
+    for name in sorted(declared_functions()):
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+        assert name in _capi.SIGNATURES, f"{name} has no ctypes signature in _capi"
+
+
+def test_struct_abi_matches():
+    lib = _capi.lib()
+    assert lib.qf_qk_norm_rope_args_size() == ctypes.sizeof(_capi.QkNormRopeArgs)
+
+
+def test_version():
+    assert _capi.lib().qf_version().decode().startswith("qwen3fused")
+
+
+def test_host_side_argument_checks_return_before_any_launch():
+    lib = _capi.lib()
+    # negative sizes / unknown dtype / null pointers: rejected on the host
+    assert lib.qf_silu_and_mul(None, 0, None, 0, None, 0, -1, 8, 2, None) == _capi.QF_ERR_INVALID
+    assert lib.qf_silu_and_mul(None, 0, None, 0, None, 0, 4, 8, 2, None) == _capi.QF_ERR_INVALID
+    assert lib.qf_rmsnorm(None, 0, None, None, 0, 4, 8, 1e-6, 9, None) == _capi.QF_ERR_INVALID
+    assert lib.qf_embedding(None, 7, None, 1, 1, None, 1, 1, 1, 2, None, None) == \
+        _capi.QF_ERR_INVALID
+    a = _capi.QkNormRopeArgs()
+    a.num_tokens, a.num_q_heads, a.num_kv_heads, a.head_dim, a.dtype = 4, 2, 1, 96, 2
+    assert lib.qf_qk_norm_rope_store(ctypes.byref(a), None) == _capi.QF_ERR_UNSUPPORTED
+    st = _capi.i64_array([0, 0, 0])
+    ct = _capi.i64_array([0, 0, 0, 0])
+    assert lib.qf_kv_store_batched(None, st, None, st, None, ct, None, ct, None, None, 1, 4, 2,
+                                   8, 2, 0, 2, None, None) == _capi.QF_ERR_INVALID
+    # zero-sized work is a no-op that needs no device
+    assert lib.qf_silu_and_mul(None, 0, None, 0, None, 0, 0, 8, 2, None) == _capi.QF_OK
+    assert lib.qf_kv_store_seq(0, None, 0, 1, None, st, None, st, None, ct, None, ct, 0, 2, 8,
+                               2, 4, 2, None, None) == _capi.QF_OK
+
+
+def test_ensure_built_is_idempotent():
+    p1 = _capi.ensure_built()
+    mtime = os.path.getmtime(p1)
+    assert _capi.ensure_built() == p1
+    assert os.path.getmtime(p1) == mtime
+
+
+@pytest.mark.parametrize("rc,exc", [(1, ValueError), (2, ValueError), (3, RuntimeError)])
+def test_return_codes_map_to_exceptions(rc, exc):
+    with pytest.raises(exc):
+        _capi.check(rc, "op")

@@ -1,0 +1,93 @@
+"""Full-size batches: size-independent properties plus oracle spot checks.
+
+c2 (14.6k tokens) and c5 (131072 tokens, Qwen3-32B widths) run at their full
+token counts; c5's cache is 400k blocks (26 GB, element offsets far past
+2^31) instead of the configuration's 120 GB so the test leaves room on a
+shared GPU.  Properties that hold at any size are checked on every element;
+the oracle checks a seeded sample of rows.
+"""
+
+import pytest
+import torch
+
+import tinyserver_b200 as tsb
+from oracle import oracle
+from tests.common import assert_close, untouched_checksum
+from tinyserver_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+CASES = {"c2": None, "c5": 400_000}
+
+
+@pytest.fixture(autouse=True)
+def _no_device_flags():
+    yield
+    tsb.check_errors()
+
+
+@pytest.fixture(scope="module", params=list(CASES))
+def batch(request):
+    b = W.make_batch(request.param, "cuda", num_blocks=CASES[request.param])
+    yield b
+    del b.tensors
+    torch.cuda.empty_cache()
+
+
+def _sample(batch, n=256):
+    g = torch.Generator().manual_seed(7)
+    return torch.randperm(batch.num_tokens, generator=g)[:n].sort().values
+
+
+def test_embedding_gathers_exact_rows(batch):
+    t = batch.tensors
+    out = tsb.embedding(t["input_ids"], t["embed_weight"])
+    assert torch.equal(out, t["embed_weight"][t["input_ids"]])
+
+
+def test_add_rmsnorm(batch):
+    t, s = batch.tensors, batch.cfg.shape
+    y, h = tsb.fused_add_rms_norm(t["attn_out"], t["residual"], t["post_attention_layernorm"],
+                                  s.eps)
+    assert torch.equal(h, t["residual"] + t["attn_out"])  # one rounding of the fp32 sum
+    rows = _sample(batch)
+    ry, rh = oracle.add_rmsnorm(t["attn_out"][rows.cuda()].cpu(), t["residual"][rows.cuda()].cpu(),
+                                t["post_attention_layernorm"].cpu(), s.eps)
+    assert_close(y[rows.cuda()], ry, "add_rmsnorm sample", min_exact=0.99)
+    # unit weight: every output row has mean square ~1 (bf16 rounding aside)
+    ones = torch.ones_like(t["post_attention_layernorm"])
+    y1 = tsb.rms_norm(h, ones, s.eps).float()
+    ms = y1.pow(2).mean(-1)
+    assert torch.allclose(ms, torch.ones_like(ms), atol=2e-2)
+
+
+def test_qk_norm_rope_store(batch):
+    t, s = batch.tensors, batch.cfg.shape
+    q, k, v = W.qkv_views(t["qkv"], s)
+    cos, sin = tsb.rope_cos_sin(t["positions"], t["inv_freq"], s.head_dim, batch.cfg.dtype)
+    assert torch.allclose((cos.float() ** 2 + sin.float() ** 2), torch.ones_like(cos.float()),
+                          atol=2e-2)
+    pool, bm, sm = t["kv_pool"], t["block_mapping"], t["slot_mapping"]
+    before = untouched_checksum(pool, bm, sm)
+    q_out, k_out = tsb.qk_norm_rope_store(q, k, v, t["q_norm"], t["k_norm"], s.eps, cos, sin,
+                                          t["k_cache"], t["v_cache"], bm, sm)
+    rows = pool[:, 0, bm, :, sm, :]
+    assert torch.equal(rows[:, 0], k_out) and torch.equal(rows[:, 1], v)
+    assert untouched_checksum(pool, bm, sm) == before
+    smp = _sample(batch).cuda()
+    rq, rk = oracle.qk_norm_rope_store(q[smp].cpu(), k[smp].cpu(), None, t["q_norm"].cpu(),
+                                       t["k_norm"].cpu(), s.eps, cos[smp].cpu(), sin[smp].cpu())
+    assert_close(q_out[smp], rq, "q sample", min_exact=0.99)
+    assert_close(k_out[smp], rk, "k sample", min_exact=0.99)
+
+
+def test_silu_and_mul(batch):
+    t = batch.tensors
+    I = batch.cfg.shape.intermediate
+    g, u = t["gate_up"][:, :I], t["gate_up"][:, I:]
+    out = tsb.silu_and_mul(t["gate_up"])
+    # sign symmetry in `up` holds exactly (negation commutes with rounding)
+    assert torch.equal(tsb.silu_and_mul(g, -u), -out)
+    smp = _sample(batch).cuda()
+    assert_close(out[smp], oracle.silu_and_mul(g[smp].cpu(), u[smp].cpu()), "silu sample",
+                 min_exact=0.99)

@@ -1,0 +1,21 @@
+"""tinyserver_b200: B200 (sm_100a) kernels for the Qwen3 decoder layer's
+memory-bound op path of tinyserver's server/model, behind its operator and
+module signatures.
+
+The kernels live in libqwen3fused.so (C ABI: include/qwen3fused.h), built
+in-tree from tinyserver_b200/csrc.  Every op runs on CUDA tensors only and
+raises otherwise; there is no CPU fallback.
+"""
+
+from ._capi import lib as load_library, lib_path
+from ._runtime import check_errors
+from .kernels import (apply_rotary_pos_emb, build_slot_mapping, embedding, fused_add_rms_norm,
+                      qk_norm_rope_store, rms_norm, rope_cos_sin, rope_inv_freq, silu_and_mul,
+                      store_kv_cache, store_kv_cache_batched)
+
+__version__ = "0.1.0"
+
+__all__ = ["apply_rotary_pos_emb", "build_slot_mapping", "check_errors", "embedding",
+           "fused_add_rms_norm", "load_library", "lib_path", "qk_norm_rope_store", "rms_norm",
+           "rope_cos_sin", "rope_inv_freq", "silu_and_mul", "store_kv_cache",
+           "store_kv_cache_batched"]
