@@ -181,13 +181,53 @@ PER_STEP_INPUTS = ["input_ids", "positions", "block_mapping", "slot_mapping", "x
                    "qkv", "attn_out", "gate_up"]
 
 
+def measure_e2e(args, step: "Step", t: dict, dev: torch.device, world: int):
+    """The step through the public API with this step's inputs copied from
+    pinned host memory and every output copied back, all inside the timed
+    region.  Returns (max-over-ranks ms, steps, H2D bytes, D2H bytes)."""
+    host_in = {k: t[k].to("cpu").pin_memory() for k in PER_STEP_INPUTS}
+    dev_in = {k: torch.empty_like(t[k]) for k in PER_STEP_INPUTS}
+    resident = {k: v for k, v in t.items() if k not in PER_STEP_INPUTS}
+    outs = step.run(t)
+    host_out = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in outs.items()}
+    h2d = sum(v.numel() * v.element_size() for v in host_in.values())
+    d2h = sum(v.numel() * v.element_size() for v in host_out.values())
+
+    def e2e_step():
+        for k in PER_STEP_INPUTS:
+            dev_in[k].copy_(host_in[k], non_blocking=True)
+        o = step.run({**resident, **dev_in})
+        for k, v in o.items():
+            host_out[k].copy_(v, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 50))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        m = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(m, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(m.item())
+        torch.distributed.barrier()
+    return e2e_ms, e2e_steps, h2d, d2h
+
+
 # ----------------------------------------------------------------------------
 def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     from tinyserver_b200 import workloads as W
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    batch = W.make_batch(CONFIG, dev, shard=rank)
+    batch = W.make_batch(CONFIG, dev, shard=rank, max_tokens=args.max_tokens)
     t = batch.tensors
     T = batch.num_tokens
     step = Step(batch)
@@ -231,39 +271,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         elapsed_ms = float(m.item())
 
     # ---- end to end from pinned host buffers ----------------------------------
-    host_in = {k: t[k].to("cpu").pin_memory() for k in PER_STEP_INPUTS}
-    dev_in = {k: torch.empty_like(t[k]) for k in PER_STEP_INPUTS}
-    resident = {k: v for k, v in t.items() if k not in PER_STEP_INPUTS}
-    outs = step.run(t)
-    host_out = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in outs.items()}
-    h2d = sum(v.numel() * v.element_size() for v in host_in.values())
-    d2h = sum(v.numel() * v.element_size() for v in host_out.values())
-
-    def e2e_step():
-        for k in PER_STEP_INPUTS:
-            dev_in[k].copy_(host_in[k], non_blocking=True)
-        o = step.run({**resident, **dev_in})
-        for k, v in o.items():
-            host_out[k].copy_(v, non_blocking=True)
-
-    e2e_steps = max(3, min(args.steps, 50))
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        m = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-        torch.distributed.all_reduce(m, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = float(m.item())
-        torch.distributed.barrier()
+    e2e = None if args.no_e2e else measure_e2e(args, step, t, dev, world)
 
     if rank != 0:
         return None
@@ -315,12 +323,18 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                      "traffic": traffic},
         "gpu_launches": nk * args.steps,
         "clocks": clocks,
-        "e2e": {"value": round(world * T * e2e_steps / (e2e_ms / 1e3), 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "steps": e2e_steps,
-                "note": "public API from pinned host buffers; every per-step input H2D and "
-                        "every output D2H inside the timed region (single stream)"},
+        "e2e": None,
     }
+    if e2e is not None:
+        e2e_ms, e2e_steps, h2d, d2h = e2e
+        line["e2e"] = {"value": round(world * T * e2e_steps / (e2e_ms / 1e3), 1),
+                       "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                       "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                       "note": "public API from pinned host buffers; every per-step input H2D "
+                               "and every output D2H inside the timed region (single stream)"}
+    if args.max_tokens is not None:
+        line["config"]["workload"] = (f"c4 prefix of {T} tokens (a profiling case, not the "
+                                      "benchmark workload)")
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(batch, budget_s=args.cpu_seconds)
     return line
@@ -458,6 +472,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
+    ap.add_argument("--max-tokens", type=int, default=None,
+                    help="keep a prefix of the batch (small profiling cases only)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU-baseline timing budget (ours arm)")
     ap.add_argument("--cpu-total", type=float, default=90.0,

@@ -131,13 +131,18 @@ def rope_cos_sin(position_ids: torch.Tensor, inv_freq: torch.Tensor, head_dim: i
                  dtype: torch.dtype, scaling: float = 1.0
                  ) -> tuple[torch.Tensor, torch.Tensor]:
     """cos/sin tables of shape ``position_ids.shape + (head_dim,)`` in ``dtype``
-    (Qwen3RotaryEmbedding.forward, default rope type)."""
+    (Qwen3RotaryEmbedding.forward, default rope type).
+
+    ``inv_freq`` may be any floating dtype: like the reference forward
+    (``self.inv_freq[None, :, None].float()``, modeling_qwen3.py:137) it is
+    upcast to float32 first, so a model cast with ``.to(bfloat16)`` (which
+    also casts the inv_freq buffer) gets the same tables as under HF."""
     itag = index_tag(position_ids, "rope_cos_sin position_ids")
     dev = require_cuda("rope_cos_sin", position_ids, inv_freq)
-    if inv_freq.dtype != torch.float32 or inv_freq.numel() != head_dim // 2:
-        raise ValueError("rope_cos_sin: inv_freq must be float32 with head_dim/2 entries")
+    if not inv_freq.is_floating_point() or inv_freq.numel() != head_dim // 2:
+        raise ValueError("rope_cos_sin: inv_freq must be floating with head_dim/2 entries")
     pos = position_ids.reshape(-1).contiguous()
-    inv = inv_freq.contiguous()
+    inv = inv_freq.to(torch.float32).contiguous()
     cos = torch.empty(*position_ids.shape, head_dim, dtype=dtype, device=dev)
     sin = torch.empty_like(cos)
     rc = _capi.lib().qf_rope_cos_sin(pos.data_ptr(), itag, inv.data_ptr(), pos.numel(),
