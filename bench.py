@@ -227,7 +227,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    batch = W.make_batch(CONFIG, dev, shard=rank, max_tokens=args.max_tokens)
+    batch = W.make_batch(CONFIG, dev, shard=rank, max_tokens=args.max_tokens,
+                         num_blocks=args.num_blocks)
     t = batch.tensors
     T = batch.num_tokens
     step = Step(batch)
@@ -332,9 +333,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                        "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                        "note": "public API from pinned host buffers; every per-step input H2D "
                                "and every output D2H inside the timed region (single stream)"}
-    if args.max_tokens is not None:
-        line["config"]["workload"] = (f"c4 prefix of {T} tokens (a profiling case, not the "
-                                      "benchmark workload)")
+    if args.max_tokens is not None or args.num_blocks is not None:
+        line["config"]["workload"] = (f"c4 prefix of {T} tokens, {batch.tensors['k_cache'].shape[0]}"
+                                      "-block cache (a profiling case, not the benchmark workload)")
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(batch, budget_s=args.cpu_seconds)
     return line
@@ -475,6 +476,8 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--max-tokens", type=int, default=None,
                     help="keep a prefix of the batch (small profiling cases only)")
+    ap.add_argument("--num-blocks", type=int, default=None,
+                    help="KV-cache blocks per GPU (small profiling cases only)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU-baseline timing budget (ours arm)")
     ap.add_argument("--cpu-total", type=float, default=90.0,

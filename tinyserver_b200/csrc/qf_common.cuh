@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "qwen3fused.h"
 
@@ -98,6 +99,159 @@ __device__ __forceinline__ uint4 pack(const float* f) {
     T* e = reinterpret_cast<T*>(&v);
 #pragma unroll
     for (int i = 0; i < Dt<T>::kPerVec; ++i) e[i] = Dt<T>::from_f(f[i]);
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// Two 16-bit values in one 32-bit register (element 0 in the low half, as in
+// memory).  The arithmetic is the IEEE round-to-nearest op of the storage
+// type with an explicit .rn (never contracted into an FMA), and it equals
+// torch's "compute in fp32, round to the dtype" for these operands:
+//  * a product of two bf16 (8-bit significands) or two fp16 (11-bit) values
+//    is exact in fp32, so rounding it once is what torch's mul does;
+//  * a sum of two such values is exact in fp32 unless their exponents differ
+//    by more than 24 - p bits; then the smaller one lies far below half an
+//    ulp of the larger, so the fp32 rounding cannot move the sum across a
+//    rounding midpoint of the 16-bit type and double rounding changes nothing.
+template <typename T>
+struct Packed;
+
+template <>
+struct Packed<__nv_bfloat16> {
+    __device__ __forceinline__ static uint32_t mul(uint32_t a, uint32_t b) {
+        uint32_t d;
+        asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+        return d;
+    }
+    __device__ __forceinline__ static uint32_t add(uint32_t a, uint32_t b) {
+        uint32_t d;
+        asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+        return d;
+    }
+    __device__ __forceinline__ static uint32_t sub(uint32_t a, uint32_t b) {
+        uint32_t d;
+        asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+        return d;
+    }
+    // round two floats to the storage type and pack them (lo at the low half)
+    __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
+        uint32_t d;
+        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+        return d;
+    }
+    __device__ __forceinline__ static float lo(uint32_t v) { return __uint_as_float(v << 16); }
+    __device__ __forceinline__ static float hi(uint32_t v) {
+        return __uint_as_float(v & 0xffff0000u);
+    }
+};
+
+template <>
+struct Packed<__half> {
+    __device__ __forceinline__ static uint32_t mul(uint32_t a, uint32_t b) {
+        uint32_t d;
+        asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+        return d;
+    }
+    __device__ __forceinline__ static uint32_t add(uint32_t a, uint32_t b) {
+        uint32_t d;
+        asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+        return d;
+    }
+    __device__ __forceinline__ static uint32_t sub(uint32_t a, uint32_t b) {
+        uint32_t d;
+        asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+        return d;
+    }
+    __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
+        uint32_t d;
+        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+        return d;
+    }
+    __device__ __forceinline__ static float lo(uint32_t v) {
+        return __half2float(__ushort_as_half((unsigned short)(v & 0xffffu)));
+    }
+    __device__ __forceinline__ static float hi(uint32_t v) {
+        return __half2float(__ushort_as_half((unsigned short)(v >> 16)));
+    }
+};
+
+__device__ __forceinline__ uint32_t word(const uint4& v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+__device__ __forceinline__ void set_word(uint4& v, int i, uint32_t w) {
+    if (i == 0) v.x = w;
+    else if (i == 1) v.y = w;
+    else if (i == 2) v.z = w;
+    else v.w = w;
+}
+
+// Sum of squares of the elements of one 16-byte vector (fp32 accumulation).
+template <typename T>
+__device__ __forceinline__ float sum_sq16(const uint4& v) {
+    float s = 0.f;
+    if constexpr (sizeof(T) == 2) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float lo = Packed<T>::lo(word(v, i)), hi = Packed<T>::hi(word(v, i));
+            s = fmaf(lo, lo, s);
+            s = fmaf(hi, hi, s);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float f = __uint_as_float(word(v, i));
+            s = fmaf(f, f, s);
+        }
+    }
+    return s;
+}
+
+// Elementwise rnd(a + b) of two 16-byte vectors (torch's same-dtype add).
+template <typename T>
+__device__ __forceinline__ uint4 add16(const uint4& a, const uint4& b) {
+    uint4 r;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if constexpr (sizeof(T) == 2)
+            set_word(r, i, Packed<T>::add(word(a, i), word(b, i)));
+        else
+            set_word(r, i, __float_as_uint(__fadd_rn(__uint_as_float(word(a, i)),
+                                                     __uint_as_float(word(b, i)))));
+    }
+    return r;
+}
+
+// Qwen3RMSNorm's scaling of one 16-byte vector: rnd(w * rnd(h * inv)).
+template <typename T>
+__device__ __forceinline__ uint4 norm16(const uint4& h, float inv, const uint4& w) {
+    uint4 r;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t hv = word(h, i);
+        if constexpr (sizeof(T) == 2) {
+            using P = Packed<T>;
+            set_word(r, i, P::mul(P::pack(__fmul_rn(P::lo(hv), inv), __fmul_rn(P::hi(hv), inv)),
+                                  word(w, i)));
+        } else {
+            set_word(r, i, __float_as_uint(__fmul_rn(__uint_as_float(word(w, i)),
+                                                     __fmul_rn(__uint_as_float(hv), inv))));
+        }
+    }
+    return r;
+}
+
+// Resident CTAs per SM of one kernel at one block size, cached per kernel
+// (the answer is fixed for a process: same kernel, same architecture).
+template <auto Kernel>
+int resident_ctas(int threads, size_t smem = 0) {
+    static std::atomic<int> cached[33];
+    const int slot = threads / 32;
+    int v = cached[slot].load(std::memory_order_relaxed);
+    if (v > 0) return v;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, Kernel, threads, smem) != cudaSuccess ||
+        v < 1)
+        v = 1;
+    cached[slot].store(v, std::memory_order_relaxed);
     return v;
 }
 

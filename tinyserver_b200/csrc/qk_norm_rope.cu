@@ -282,6 +282,232 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const QkDev a) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// 16-byte path (the serving layout: every row start and stride 16-byte
+// aligned).  A head row of D elements is split over G = D / (2 * EPV) lanes;
+// lane l holds the 16-byte vector l of the first half and vector l of the
+// second half, so the neox pairs (i, i + D/2) are again in one lane.  Each
+// lane keeps U head rows in flight (4 x 2 x 16 bytes), the norm weights sit in
+// shared memory, and for 16-bit types the norm's weight multiply and all of
+// RoPE run as packed .rn bf16x2/f16x2 ops (see Packed), which round exactly
+// where torch's separate mul/add kernels round.
+template <typename T, int D>
+struct VecRow {
+    static constexpr int EPV = 16 / (int)sizeof(T);  // elements per 16-byte vector
+    static constexpr int G = D / (2 * EPV);          // lanes per head row
+    static constexpr int HPW = 32 / G;               // head rows per warp step
+    static constexpr int U = 4;                      // warp steps in flight
+    static_assert(G >= 1 && G <= 32 && (G & (G - 1)) == 0, "unsupported head_dim");
+};
+
+// norm + RoPE of one head row held as two 16-byte vectors (x1: first half, x2:
+// second half); w1/w2 the weight vectors, c1/c2/s1/s2 the cos/sin vectors.
+template <typename T>
+__device__ __forceinline__ void norm_rope_vec(uint4& x1, uint4& x2, bool has_w, float inv,
+                                              const uint4& w1, const uint4& w2, const uint4& c1,
+                                              const uint4& c2, const uint4& s1,
+                                              const uint4& s2) {
+    if constexpr (sizeof(T) == 2) {
+        using P = Packed<T>;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            uint32_t a = word(x1, i), b = word(x2, i);
+            if (has_w) {
+                a = P::mul(P::pack(__fmul_rn(P::lo(a), inv), __fmul_rn(P::hi(a), inv)),
+                           word(w1, i));
+                b = P::mul(P::pack(__fmul_rn(P::lo(b), inv), __fmul_rn(P::hi(b), inv)),
+                           word(w2, i));
+            }
+            // out1 = x1*cos1 - x2*sin1 ; out2 = x2*cos2 + x1*sin2   (rotate_half)
+            set_word(x1, i, P::sub(P::mul(a, word(c1, i)), P::mul(b, word(s1, i))));
+            set_word(x2, i, P::add(P::mul(b, word(c2, i)), P::mul(a, word(s2, i))));
+        }
+    } else {
+        const float* fx1 = reinterpret_cast<const float*>(&x1);
+        const float* fx2 = reinterpret_cast<const float*>(&x2);
+        const float* fw1 = reinterpret_cast<const float*>(&w1);
+        const float* fw2 = reinterpret_cast<const float*>(&w2);
+        const float* fc1 = reinterpret_cast<const float*>(&c1);
+        const float* fc2 = reinterpret_cast<const float*>(&c2);
+        const float* fs1 = reinterpret_cast<const float*>(&s1);
+        const float* fs2 = reinterpret_cast<const float*>(&s2);
+        float o1[4], o2[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float a = fx1[i], b = fx2[i];
+            if (has_w) {
+                a = __fmul_rn(fw1[i], __fmul_rn(a, inv));
+                b = __fmul_rn(fw2[i], __fmul_rn(b, inv));
+            }
+            o1[i] = __fadd_rn(__fmul_rn(a, fc1[i]), __fmul_rn(-b, fs1[i]));
+            o2[i] = __fadd_rn(__fmul_rn(b, fc2[i]), __fmul_rn(a, fs2[i]));
+        }
+        x1 = make_uint4(__float_as_uint(o1[0]), __float_as_uint(o1[1]), __float_as_uint(o1[2]),
+                        __float_as_uint(o1[3]));
+        x2 = make_uint4(__float_as_uint(o2[0]), __float_as_uint(o2[1]), __float_as_uint(o2[2]),
+                        __float_as_uint(o2[3]));
+    }
+}
+
+// cos/sin vectors of EPV frequencies starting at j0, computed from the
+// position exactly as the table would hold them (rounded to T).
+template <typename T>
+__device__ __forceinline__ void cos_sin_vec(const float* inv_freq, int j0, float p, uint4& c,
+                                            uint4& s) {
+    constexpr int EPV = 16 / (int)sizeof(T);
+    float cv[EPV], sv[EPV];
+#pragma unroll
+    for (int j = 0; j < EPV; ++j) sincosf(__fmul_rn(__ldg(inv_freq + j0 + j), p), &sv[j], &cv[j]);
+    c = pack<T>(cv);
+    s = pack<T>(sv);
+}
+
+template <typename T, int D, typename IT>
+__global__ void __launch_bounds__(256, 3) qk_norm_rope_vec_kernel(const QkDev a) {
+    using R = VecRow<T, D>;
+    constexpr int EPV = R::EPV, G = R::G, HPW = R::HPW, U = R::U;
+    constexpr int HALF = D / 2;
+    constexpr int64_t ES = sizeof(T);
+    constexpr int NV = D * (int)ES / 16;  // 16-byte vectors per weight vector
+
+    __shared__ uint4 wsm[2][NV];  // q_norm and k_norm weights
+    for (int i = threadIdx.x; i < 2 * NV; i += blockDim.x) {
+        const char* w = i < NV ? a.qw : a.kw;
+        const int j = i < NV ? i : i - NV;
+        wsm[i < NV ? 0 : 1][j] = w ? ld_shared_ro16(w + j * 16) : make_uint4(0, 0, 0, 0);
+    }
+    __syncthreads();
+
+    const int lane = threadIdx.x & 31;
+    const int sub = lane / G;
+    const int gl = lane - sub * G;
+    const int e0 = gl * EPV;
+    const int64_t off1 = e0 * ES, off2 = (HALF + e0) * ES;
+
+    const IT tpt = (IT)a.tasks_per_token;
+    const IT total = (IT)a.T * tpt;
+    const IT warp = ((IT)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const IT nwarp = ((IT)gridDim.x * blockDim.x) >> 5;
+    const IT Hq = (IT)a.Hq, Hkv = (IT)a.Hkv;
+
+    for (IT base = warp * (HPW * U); base < total; base += nwarp * (HPW * U)) {
+        uint4 r1[U], r2[U];
+        int64_t tt[U], hh[U];
+        int kind[U];
+        bool act[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const IT task = base + (IT)(u * HPW + sub);
+            act[u] = task < total;
+            const IT t = act[u] ? task / tpt : 0;
+            const IT hx = act[u] ? task - t * tpt : 0;
+            tt[u] = (int64_t)t;
+            const char* src;
+            if (hx < Hq) {
+                kind[u] = 0;
+                hh[u] = (int64_t)hx;
+                src = a.q + (tt[u] * a.q_st + hh[u] * a.q_sh) * ES;
+            } else if (hx < Hq + Hkv) {
+                kind[u] = 1;
+                hh[u] = (int64_t)(hx - Hq);
+                src = a.k + (tt[u] * a.k_st + hh[u] * a.k_sh) * ES;
+            } else {
+                kind[u] = 2;
+                hh[u] = (int64_t)(hx - Hq - Hkv);
+                src = a.v + (tt[u] * a.v_st + hh[u] * a.v_sh) * ES;
+            }
+            if (act[u]) {
+                r1[u] = ld_stream16(src + off1);
+                r2[u] = ld_stream16(src + off2);
+            }
+        }
+
+        float ss[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            ss[u] = 0.f;
+            const bool has_w = kind[u] == 0 ? a.qw != nullptr : a.kw != nullptr;
+            if (act[u] && kind[u] < 2 && has_w) ss[u] = sum_sq16<T>(r1[u]) + sum_sq16<T>(r2[u]);
+        }
+        // every lane runs every shuffle: the G-lane groups reduce side by side
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+#pragma unroll
+            for (int o = G / 2; o > 0; o >>= 1) ss[u] += __shfl_xor_sync(0xffffffffu, ss[u], o);
+        }
+
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            if (!act[u]) continue;
+            const int64_t t = tt[u], h = hh[u];
+            if (kind[u] == 2) {  // V row: bit-exact copy into its page
+                int64_t blk, slot;
+                if (cache_slot(a, t, blk, slot, gl == 0 && h == 0)) {
+                    char* dst = a.v_cache + (blk * a.c0 + h * a.c1 + slot * a.c2) * ES;
+                    st16(dst + off1, r1[u]);
+                    st16(dst + off2, r2[u]);
+                }
+                continue;
+            }
+            const bool is_q = kind[u] == 0;
+            const bool has_w = is_q ? a.qw != nullptr : a.kw != nullptr;
+            const float inv = has_w ? inv_rms(ss[u], D, a.eps) : 1.f;
+            uint4 c1, c2, s1, s2;
+            if (a.cos) {
+                const char* cr = a.cos + t * a.cs_st * ES;
+                const char* sr = a.sin + t * a.cs_st * ES;
+                c1 = ld_shared_ro16(cr + off1);
+                c2 = ld_shared_ro16(cr + off2);
+                s1 = ld_shared_ro16(sr + off1);
+                s2 = ld_shared_ro16(sr + off2);
+            } else {
+                cos_sin_vec<T>(a.inv_freq, e0, (float)load_index(a.pos, t, a.pos_type), c1, s1);
+                c2 = c1;
+                s2 = s1;
+            }
+            const uint4* w = wsm[is_q ? 0 : 1];
+            norm_rope_vec<T>(r1[u], r2[u], has_w, inv, w[gl], w[NV / 2 + gl], c1, c2, s1, s2);
+            if (is_q) {
+                char* dst = a.q_out + (t * a.qo_st + h * a.qo_sh) * ES;
+                st16(dst + off1, r1[u]);
+                st16(dst + off2, r2[u]);
+            } else {
+                if (a.k_out) {
+                    char* dst = a.k_out + (t * a.ko_st + h * a.ko_sh) * ES;
+                    st16(dst + off1, r1[u]);
+                    st16(dst + off2, r2[u]);
+                }
+                int64_t blk, slot;
+                if (a.store && cache_slot(a, t, blk, slot, gl == 0 && h == 0)) {
+                    char* dst = a.k_cache + (blk * a.c0 + h * a.c1 + slot * a.c2) * ES;
+                    st16(dst + off1, r1[u]);
+                    st16(dst + off2, r2[u]);
+                }
+            }
+        }
+    }
+}
+
+template <typename T, int D, typename IT>
+int launch_qk_vec_it(const QkDev& a, cudaStream_t stream) {
+    using R = VecRow<T, D>;
+    constexpr auto kernel = qk_norm_rope_vec_kernel<T, D, IT>;
+    const int threads = 256;
+    const int64_t total = a.T * a.tasks_per_token;
+    const int64_t warps = ceil_div(total, (int64_t)R::HPW * R::U);
+    const int64_t need = ceil_div(warps, threads / 32);
+    const int64_t fill = (int64_t)sm_count() * resident_ctas<kernel>(threads);
+    kernel<<<(unsigned)std::min<int64_t>(need, fill), threads, 0, stream>>>(a);
+    return check_launch();
+}
+
+template <typename T, int D>
+int launch_qk_vec(const QkDev& a, cudaStream_t stream) {
+    if (a.T * a.tasks_per_token < (int64_t(1) << 31))
+        return launch_qk_vec_it<T, D, uint32_t>(a, stream);
+    return launch_qk_vec_it<T, D, uint64_t>(a, stream);
+}
+
 template <typename T, int D>
 int launch_qk(const QkDev& a, cudaStream_t stream) {
     constexpr int G = D / 8, HPW = 32 / G, U = 2;
@@ -297,11 +523,11 @@ int launch_qk(const QkDev& a, cudaStream_t stream) {
 }
 
 template <typename T>
-int dispatch_qk(const QkDev& a, int64_t D, cudaStream_t stream) {
+int dispatch_qk(const QkDev& a, int64_t D, bool vec, cudaStream_t stream) {
     switch (D) {
-    case 64: return launch_qk<T, 64>(a, stream);
-    case 128: return launch_qk<T, 128>(a, stream);
-    case 256: return launch_qk<T, 256>(a, stream);
+    case 64: return vec ? launch_qk_vec<T, 64>(a, stream) : launch_qk<T, 64>(a, stream);
+    case 128: return vec ? launch_qk_vec<T, 128>(a, stream) : launch_qk<T, 128>(a, stream);
+    case 256: return vec ? launch_qk_vec<T, 256>(a, stream) : launch_qk<T, 256>(a, stream);
     default: return QF_ERR_UNSUPPORTED;
     }
 }
@@ -376,6 +602,13 @@ extern "C" int qf_qk_norm_rope_store(const qf_qk_norm_rope_args* p, cudaStream_t
                           store ? g.v : nullptr, g.k_cache, g.v_cache};
     for (const void* ptr : ptrs)
         if (ptr && !qf::al(ptr, qa)) return QF_ERR_UNSUPPORTED;
+    // the 16-byte path when every row start is 16-byte aligned (the serving
+    // layout); otherwise the 4-element path above
+    bool vec = true;
+    for (int64_t s : strides)
+        if ((s * es) % 16) vec = false;
+    for (const void* ptr : ptrs)
+        if (ptr && !qf::al(ptr, 16)) vec = false;
 
     qf::QkDev a{};
     a.q = static_cast<const char*>(g.q);
@@ -419,9 +652,9 @@ extern "C" int qf_qk_norm_rope_store(const qf_qk_norm_rope_args* p, cudaStream_t
     a.tasks_per_token = g.num_q_heads + g.num_kv_heads + (store ? g.num_kv_heads : 0);
     a.status = g.status;
     switch (g.dtype) {
-    case QF_F32: return qf::dispatch_qk<float>(a, D, stream);
-    case QF_F16: return qf::dispatch_qk<__half>(a, D, stream);
-    default: return qf::dispatch_qk<__nv_bfloat16>(a, D, stream);
+    case QF_F32: return qf::dispatch_qk<float>(a, D, vec, stream);
+    case QF_F16: return qf::dispatch_qk<__half>(a, D, vec, stream);
+    default: return qf::dispatch_qk<__nv_bfloat16>(a, D, vec, stream);
     }
 }
 

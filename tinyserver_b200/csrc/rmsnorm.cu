@@ -10,8 +10,6 @@
 // CTAs are persistent (grid = min(rows, resident CTAs)) and keep the weight
 // vector in registers for every row they process.  Rounding follows the
 // reference op by op: h = rnd(res + x); y = rnd(w * rnd(h * rsqrt(var + eps))).
-#include <atomic>
-
 #include "qf_common.cuh"
 
 namespace qf {
@@ -45,43 +43,58 @@ __device__ __forceinline__ float inv_rms(float sum_sq, int64_t H, float eps) {
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
 }
 
-// Rows up to 1024 vectors use <= 256 threads (VPT <= 4); only VPT 8 needs 1024.
+// One CTA per row at a time, persistent over rows.  Thread i holds vectors
+// i, i + nthr, ... of the row (VPT of them) as raw 16-byte words; the weight
+// stays in registers for every row.  The next row's loads are issued before
+// the current row's block reduction, so a CTA always has a row in flight
+// while it reduces, scales and stores the previous one.  16-bit types add and
+// scale with packed .rn ops (see Packed): the same roundings as torch's
+// separate add, cast and mul kernels.
 template <typename T, int VPT, bool ADD>
-__global__ void __launch_bounds__(VPT == 8 ? 1024 : 256) rmsnorm_vec_kernel(const NormArgs a) {
-    constexpr int EPV = Dt<T>::kPerVec;
+__global__ void __launch_bounds__(VPT == 8 ? 512 : 256) rmsnorm_vec_kernel(const NormArgs a) {
     __shared__ float red[2][32];
     const int tid = threadIdx.x;
     const int nthr = blockDim.x;
     const int lane = tid & 31, warp = tid >> 5, nwarps = nthr >> 5;
+    constexpr int64_t ES = sizeof(T);
 
-    float w[VPT][EPV];
+    uint4 w[VPT];
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
         const int64_t v = tid + (int64_t)j * nthr;
-        if (v < a.nvec) unpack<T>(ld_shared_ro16(a.w + v * 16), w[j]);
+        w[j] = v < a.nvec ? ld_shared_ro16(a.w + v * 16) : make_uint4(0, 0, 0, 0);
     }
 
-    int parity = 0;
-    for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x, parity ^= 1) {
-        const char* xr = a.x + row * a.xs * (int64_t)sizeof(T);
-        const char* rr = ADD ? a.res + row * a.rs * (int64_t)sizeof(T) : nullptr;
-        float h[VPT][EPV];
-        float ss = 0.f;
+    uint4 xr[VPT], rr[VPT];
+    auto load_row = [&](int64_t row) {
+        const char* xp = a.x + row * a.xs * ES;
+        const char* rp = ADD ? a.res + row * a.rs * ES : nullptr;
 #pragma unroll
         for (int j = 0; j < VPT; ++j) {
             const int64_t v = tid + (int64_t)j * nthr;
             if (v < a.nvec) {
-                unpack<T>(ld_stream16(xr + v * 16), h[j]);
-                if (ADD) {
-                    float r[EPV];
-                    unpack<T>(ld_stream16(rr + v * 16), r);
-#pragma unroll
-                    for (int e = 0; e < EPV; ++e) h[j][e] = rnd<T>(__fadd_rn(r[e], h[j][e]));
-                }
-#pragma unroll
-                for (int e = 0; e < EPV; ++e) ss = fmaf(h[j][e], h[j][e], ss);
+                xr[j] = ld_stream16(xp + v * 16);
+                if (ADD) rr[j] = ld_stream16(rp + v * 16);
             }
         }
+    };
+
+    int64_t row = blockIdx.x;
+    if (row < a.rows) load_row(row);
+    for (int parity = 0; row < a.rows; row += gridDim.x, parity ^= 1) {
+        uint4 h[VPT];
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < VPT; ++j) {
+            const int64_t v = tid + (int64_t)j * nthr;
+            h[j] = make_uint4(0, 0, 0, 0);
+            if (v < a.nvec) {
+                h[j] = ADD ? add16<T>(rr[j], xr[j]) : xr[j];
+                ss += sum_sq16<T>(h[j]);
+            }
+        }
+        // prefetch: this CTA's next row is in flight during the reduction
+        if (row + gridDim.x < a.rows) load_row(row + gridDim.x);
         ss = warp_sum(ss);
         if (lane == 0) red[parity][warp] = ss;
         __syncthreads();
@@ -89,18 +102,14 @@ __global__ void __launch_bounds__(VPT == 8 ? 1024 : 256) rmsnorm_vec_kernel(cons
         for (int i = 0; i < nwarps; ++i) tot += red[parity][i];
         const float inv = inv_rms(tot, a.H, a.eps);
 
-        char* outr = a.out + row * a.os * (int64_t)sizeof(T);
-        char* rout = ADD ? a.res_out + row * a.ros * (int64_t)sizeof(T) : nullptr;
+        char* outr = a.out + row * a.os * ES;
+        char* rout = ADD ? a.res_out + row * a.ros * ES : nullptr;
 #pragma unroll
         for (int j = 0; j < VPT; ++j) {
             const int64_t v = tid + (int64_t)j * nthr;
             if (v < a.nvec) {
-                float y[EPV];
-#pragma unroll
-                for (int e = 0; e < EPV; ++e)
-                    y[e] = __fmul_rn(w[j][e], rnd<T>(__fmul_rn(h[j][e], inv)));
-                if (ADD) st16(rout + v * 16, pack<T>(h[j]));
-                st16(outr + v * 16, pack<T>(y));
+                if (ADD) st16(rout + v * 16, h[j]);
+                st16(outr + v * 16, norm16<T>(h[j], inv, w[j]));
             }
         }
     }
@@ -137,26 +146,11 @@ __global__ void __launch_bounds__(256) rmsnorm_scalar_kernel(const NormArgs a) {
     }
 }
 
-// Resident CTAs per SM for one kernel instance and block size (cached: the
-// answer depends only on the kernel and the architecture).
-template <typename T, int VPT, bool ADD>
-int resident_per_sm(int threads) {
-    static std::atomic<int> cache[33];
-    const int slot = threads / 32;
-    int v = cache[slot].load(std::memory_order_relaxed);
-    if (v > 0) return v;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, rmsnorm_vec_kernel<T, VPT, ADD>,
-                                                      threads, 0) != cudaSuccess ||
-        v < 1)
-        v = 1;
-    cache[slot].store(v, std::memory_order_relaxed);
-    return v;
-}
-
 template <typename T, int VPT, bool ADD>
 int launch_vec(const NormArgs& a, cudaStream_t stream) {
-    const int threads = (int)std::min<int64_t>(1024, ceil_div(ceil_div(a.nvec, VPT), 32) * 32);
-    const int per_sm = resident_per_sm<T, VPT, ADD>(threads);
+    const int threads = (int)std::min<int64_t>(VPT == 8 ? 512 : 256,
+                                               ceil_div(ceil_div(a.nvec, VPT), 32) * 32);
+    const int per_sm = resident_ctas<rmsnorm_vec_kernel<T, VPT, ADD>>(threads);
     const int64_t grid = std::min<int64_t>(a.rows, (int64_t)sm_count() * per_sm);
     rmsnorm_vec_kernel<T, VPT, ADD><<<(unsigned)grid, threads, 0, stream>>>(a);
     return check_launch();
@@ -177,7 +171,7 @@ int dispatch(NormArgs& a, cudaStream_t stream) {
         if (a.nvec <= 256) return launch_vec<T, 1, ADD>(a, stream);
         if (a.nvec <= 512) return launch_vec<T, 2, ADD>(a, stream);
         if (a.nvec <= 1024) return launch_vec<T, 4, ADD>(a, stream);
-        if (a.nvec <= 8192) return launch_vec<T, 8, ADD>(a, stream);
+        if (a.nvec <= 4096) return launch_vec<T, 8, ADD>(a, stream);
     }
     if (a.rows > 0x7fffffffLL) return QF_ERR_UNSUPPORTED;
     rmsnorm_scalar_kernel<T, ADD><<<(unsigned)a.rows, 256, 0, stream>>>(a);

@@ -34,11 +34,30 @@ __device__ __forceinline__ float silu<float>(float g) {
     return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
 }
 
+// rnd(rnd(silu(g)) * u) on one 16-byte vector; 16-bit types multiply with a
+// packed .rn op (the product of two 16-bit values is exact in fp32, so one
+// rounding is what torch's mul does).
+template <typename T>
+__device__ __forceinline__ uint4 silu_mul16(const uint4& g, const uint4& u) {
+    uint4 r;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t gw = word(g, i);
+        if constexpr (sizeof(T) == 2) {
+            using P = Packed<T>;
+            set_word(r, i, P::mul(P::pack(silu<T>(P::lo(gw)), silu<T>(P::hi(gw))), word(u, i)));
+        } else {
+            set_word(r, i, __float_as_uint(__fmul_rn(silu<T>(__uint_as_float(gw)),
+                                                     __uint_as_float(word(u, i)))));
+        }
+    }
+    return r;
+}
+
 // blockIdx.x enumerates (row, chunk); a chunk is blockDim.x * VPT vectors.
 template <typename T, int VPT>
 __global__ void __launch_bounds__(256) silu_mul_vec_kernel(const SiluArgs a, const int64_t nvec,
                                                            const int64_t chunks) {
-    constexpr int EPV = Dt<T>::kPerVec;
     const int64_t row = blockIdx.x / chunks;
     const int64_t chunk = blockIdx.x - row * chunks;
     const char* g = a.gate + row * a.gs * (int64_t)sizeof(T);
@@ -57,14 +76,7 @@ __global__ void __launch_bounds__(256) silu_mul_vec_kernel(const SiluArgs a, con
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
         const int64_t v = v0 + (int64_t)j * blockDim.x;
-        if (v < nvec) {
-            float gf[EPV], uf[EPV], of[EPV];
-            unpack<T>(gv[j], gf);
-            unpack<T>(uv[j], uf);
-#pragma unroll
-            for (int e = 0; e < EPV; ++e) of[e] = __fmul_rn(rnd<T>(silu<T>(gf[e])), uf[e]);
-            st_stream16(o + v * 16, pack<T>(of));
-        }
+        if (v < nvec) st_stream16(o + v * 16, silu_mul16<T>(gv[j], uv[j]));
     }
 }
 
