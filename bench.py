@@ -11,9 +11,9 @@ GPU, positions < 32768, a 65536-block (16-token page) KV cache per GPU, seeded
 synthetic inputs with 0.1% x50 outliers.  One step is one pass of the path
 over the batch, in the decoder layer's order:
 
-  embedding gather -> residual add + input RMSNorm -> RoPE cos/sin ->
-  q_norm/k_norm + RoPE + paged KV store -> residual add + post-attn RMSNorm ->
-  SiLU-and-mul
+  embedding gather -> residual add + input RMSNorm ->
+  q_norm/k_norm + RoPE (cos/sin computed in the kernel from the positions) +
+  paged KV store -> residual add + post-attn RMSNorm -> SiLU-and-mul
 
 (the GEMMs between them are outside the path; their outputs are seeded
 inputs).  Ranks shard tokens (weak scaling, no collective on the timed path).
@@ -122,8 +122,8 @@ class ClockSampler:
 class Step:
     """One fused-layer pass over one GPU's batch, through the public API."""
 
-    KERNELS = ["embedding", "add_rmsnorm_in", "rope_cos_sin", "qk_norm_rope_store",
-               "add_rmsnorm_post", "silu_and_mul"]
+    KERNELS = ["embedding", "add_rmsnorm_in", "qk_norm_rope_store", "add_rmsnorm_post",
+               "silu_and_mul"]
 
     def __init__(self, batch):
         import tinyserver_b200 as tsb
@@ -146,32 +146,27 @@ class Step:
         y1, h1 = tsb.fused_add_rms_norm(t["x_mlp"], x0, t["input_layernorm"], s.eps)
         if ev is not None:
             ev[2].record()
-        cos, sin = tsb.rope_cos_sin(t["positions"], t["inv_freq"], s.head_dim, self.dt)
+        q, k, v = self.W.qkv_views(t["qkv"], s)
+        q_out, _ = tsb.qk_norm_rope_store(q, k, v, t["q_norm"], t["k_norm"], s.eps, None, None,
+                                          t["k_cache"], t["v_cache"], t["block_mapping"],
+                                          t["slot_mapping"], positions=t["positions"],
+                                          inv_freq=t["inv_freq"], want_k_out=False)
         if ev is not None:
             ev[3].record()
-        q, k, v = self.W.qkv_views(t["qkv"], s)
-        q_out, _ = tsb.qk_norm_rope_store(q, k, v, t["q_norm"], t["k_norm"], s.eps, cos, sin,
-                                          t["k_cache"], t["v_cache"], t["block_mapping"],
-                                          t["slot_mapping"], want_k_out=False)
-        if ev is not None:
-            ev[4].record()
         y2, h2 = tsb.fused_add_rms_norm(t["attn_out"], h1, t["post_attention_layernorm"], s.eps)
         if ev is not None:
-            ev[5].record()
+            ev[4].record()
         act = tsb.silu_and_mul(t["gate_up"])
         if ev is not None:
-            ev[6].record()
+            ev[5].record()
         return {"normed_in": y1, "q": q_out, "normed_post": y2, "residual": h2, "act": act}
 
     def bytes_per_token(self) -> dict[str, int]:
         bpt = self.W.bytes_per_token(self.s)
-        D = self.s.head_dim
-        elem = torch.tensor([], dtype=self.dt).element_size()
         return {
             "embedding": bpt["embedding"],
             "add_rmsnorm_in": bpt["add_rmsnorm"],
-            "rope_cos_sin": 2 * D * elem + 8,                       # cos+sin rows out, position in
-            "qk_norm_rope_store": bpt["qk_norm_rope_store"] + 2 * D * elem,  # + cos/sin table rows
+            "qk_norm_rope_store": bpt["qk_norm_rope_store"],  # cos/sin computed, not read
             "add_rmsnorm_post": bpt["add_rmsnorm"],
             "silu_and_mul": bpt["silu_and_mul"],
         }

@@ -9,6 +9,9 @@
 
 #include <algorithm>
 #include <atomic>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "qwen3fused.h"
 
@@ -240,18 +243,23 @@ __device__ __forceinline__ uint4 norm16(const uint4& h, float inv, const uint4& 
     return r;
 }
 
-// Resident CTAs per SM of one kernel at one block size, cached per kernel
-// (the answer is fixed for a process: same kernel, same architecture).
+// Resident CTAs per SM of one kernel at one block size and dynamic shared
+// memory size, cached per kernel (fixed for a process on one architecture).
 template <auto Kernel>
 int resident_ctas(int threads, size_t smem = 0) {
-    static std::atomic<int> cached[33];
-    const int slot = threads / 32;
-    int v = cached[slot].load(std::memory_order_relaxed);
-    if (v > 0) return v;
+    static std::mutex mu;
+    static std::map<std::pair<int, size_t>, int> cache;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = cache.find({threads, smem});
+        if (it != cache.end()) return it->second;
+    }
+    int v = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, Kernel, threads, smem) != cudaSuccess ||
         v < 1)
         v = 1;
-    cached[slot].store(v, std::memory_order_relaxed);
+    std::lock_guard<std::mutex> lock(mu);
+    cache[{threads, smem}] = v;
     return v;
 }
 

@@ -284,20 +284,38 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const QkDev a) {
 
 // ---------------------------------------------------------------------------
 // 16-byte path (the serving layout: every row start and stride 16-byte
-// aligned).  A head row of D elements is split over G = D / (2 * EPV) lanes;
-// lane l holds the 16-byte vector l of the first half and vector l of the
-// second half, so the neox pairs (i, i + D/2) are again in one lane.  Each
-// lane keeps U head rows in flight (4 x 2 x 16 bytes), the norm weights sit in
-// shared memory, and for 16-bit types the norm's weight multiply and all of
-// RoPE run as packed .rn bf16x2/f16x2 ops (see Packed), which round exactly
-// where torch's separate mul/add kernels round.
+// aligned).  Work unit = (token, step): HPW consecutive head rows of one
+// token from its row list [q heads | k heads | v heads when storing].  A head
+// row is split over G lanes (2 for 16-bit D <= 256); lane g of a row holds the
+// 16-byte chunks g, g + G, g + 2G, ... of the first half and the same chunks
+// of the second half, so
+//  * the neox pairs (i, i + D/2) of the rotation are in one lane,
+//  * the G lanes of a row touch G adjacent chunks per instruction (whole
+//    32-byte sectors for G = 2),
+//  * the RMS reduction is log2(G) shuffles, and
+//  * everything that depends only on the token (row bases, the cos/sin row,
+//    the cache slot) is set up once per unit and shared by HPW rows.
+// For 16-bit types the norm's weight multiply and all of RoPE run as packed
+// .rn ops (see Packed), which round exactly where torch's separate kernels do.
+// Lanes per head row and the CTAs per SM the register budget is sized for
+// (compile-time knobs; the defaults are the best of a sweep on B200 at
+// Qwen3-8B shapes: 2, 4 and 8 lanes per row, with and without prefetching).
+#ifndef QF_QK_LANES
+#define QF_QK_LANES 4
+#endif
+#ifndef QF_QK_MIN_CTAS
+#define QF_QK_MIN_CTAS 3
+#endif
+
 template <typename T, int D>
-struct VecRow {
-    static constexpr int EPV = 16 / (int)sizeof(T);  // elements per 16-byte vector
-    static constexpr int G = D / (2 * EPV);          // lanes per head row
+struct Wide {
+    static constexpr int EPV = 16 / (int)sizeof(T);  // elements per 16-byte chunk
+    static constexpr int NCH = D / 2 / EPV;          // chunks per half row
+    static constexpr int G0 = QF_QK_LANES < NCH ? QF_QK_LANES : NCH;
+    static constexpr int G = NCH / 8 > G0 ? NCH / 8 : G0;  // lanes per row
+    static constexpr int C = NCH / G;                // chunk pairs per lane
     static constexpr int HPW = 32 / G;               // head rows per warp step
-    static constexpr int U = 4;                      // warp steps in flight
-    static_assert(G >= 1 && G <= 32 && (G & (G - 1)) == 0, "unsupported head_dim");
+    static_assert(NCH % G == 0 && C >= 1 && C <= 8, "unsupported head_dim");
 };
 
 // norm + RoPE of one head row held as two 16-byte vectors (x1: first half, x2:
@@ -349,28 +367,152 @@ __device__ __forceinline__ void norm_rope_vec(uint4& x1, uint4& x2, bool has_w, 
     }
 }
 
-// cos/sin vectors of EPV frequencies starting at j0, computed from the
-// position exactly as the table would hold them (rounded to T).
-template <typename T>
-__device__ __forceinline__ void cos_sin_vec(const float* inv_freq, int j0, float p, uint4& c,
-                                            uint4& s) {
-    constexpr int EPV = 16 / (int)sizeof(T);
-    float cv[EPV], sv[EPV];
-#pragma unroll
-    for (int j = 0; j < EPV; ++j) sincosf(__fmul_rn(__ldg(inv_freq + j0 + j), p), &sv[j], &cv[j]);
-    c = pack<T>(cv);
-    s = pack<T>(sv);
+// 1 / sqrt(mean(x^2) + eps) with the same IEEE roundings as inv_rms, cheaper:
+// for a power-of-two D the division by D is an exact multiply, and a
+// correctly rounded reciprocal equals the correctly rounded 1/x division.
+template <int D>
+__device__ __forceinline__ float inv_rms_pow2(float sum_sq, float eps) {
+    static_assert((D & (D - 1)) == 0, "D must be a power of two");
+    return __frcp_rn(__fsqrt_rn(__fadd_rn(sum_sq * (1.0f / D), eps)));
 }
 
-template <typename T, int D, typename IT>
-__global__ void __launch_bounds__(256, 3) qk_norm_rope_vec_kernel(const QkDev a) {
-    using R = VecRow<T, D>;
-    constexpr int EPV = R::EPV, G = R::G, HPW = R::HPW, U = R::U;
-    constexpr int HALF = D / 2;
-    constexpr int64_t ES = sizeof(T);
-    constexpr int NV = D * (int)ES / 16;  // 16-byte vectors per weight vector
+// Per-warp staging of one token's cos and sin rows in shared memory (layout
+// cos[0:D] | sin[0:D]): copied from the table, or computed in the kernel with
+// each frequency evaluated once (cos[i] = cos[i + D/2], as the table built by
+// cat(freqs, freqs) holds it).
+template <typename T, int D>
+__device__ __forceinline__ void stage_cos_sin(uint4* cs, const char* cos_row,
+                                              const char* sin_row, const float* inv_freq,
+                                              float p, int lane) {
+    constexpr int NCHR = D * (int)sizeof(T) / 16;  // chunks per full row
+    if (cos_row) {
+        for (int i = lane; i < 2 * NCHR; i += 32)
+            cs[i] = ld_shared_ro16(i < NCHR ? cos_row + i * 16 : sin_row + (i - NCHR) * 16);
+    } else {
+        constexpr int HALF = D / 2;
+        T* e = reinterpret_cast<T*>(cs);
+        for (int j = lane; j < HALF; j += 32) {
+            float sv, cv;
+            sincosf(__fmul_rn(__ldg(inv_freq + j), p), &sv, &cv);
+            e[j] = e[HALF + j] = Dt<T>::from_f(cv);
+            e[D + j] = e[D + HALF + j] = Dt<T>::from_f(sv);
+        }
+    }
+}
 
-    __shared__ uint4 wsm[2][NV];  // q_norm and k_norm weights
+// One unit's rows in registers, and where they came from.
+template <typename T, int D>
+struct UnitRows {
+    uint4 x1[Wide<T, D>::C], x2[Wide<T, D>::C];
+    int64_t t;
+    int kind;  // 0 q, 1 k, 2 v, 3 past the last row
+    int h;
+};
+
+template <typename T, int D, typename IT>
+__device__ __forceinline__ void load_unit(const QkDev& a, IT unit, IT steps, int sub, int gl,
+                                          UnitRows<T, D>& u) {
+    using W = Wide<T, D>;
+    constexpr int64_t ES = sizeof(T);
+    const IT tu = unit / steps;
+    u.t = (int64_t)tu;
+    const int row = (int)(unit - tu * steps) * W::HPW + sub;
+    const int Hq = (int)a.Hq, Hkv = (int)a.Hkv;
+    u.kind = row < Hq ? 0 : row < Hq + Hkv ? 1 : row < (int)a.tasks_per_token ? 2 : 3;
+    u.h = u.kind == 0 ? row : u.kind == 1 ? row - Hq : row - Hq - Hkv;
+    const char* src = u.kind == 0   ? a.q + (u.t * a.q_st + (int64_t)u.h * a.q_sh) * ES
+                      : u.kind == 1 ? a.k + (u.t * a.k_st + (int64_t)u.h * a.k_sh) * ES
+                                    : a.v + (u.t * a.v_st + (int64_t)u.h * a.v_sh) * ES;
+    if (u.kind < 3) {
+#pragma unroll
+        for (int m = 0; m < W::C; ++m) {
+            u.x1[m] = ld_stream16(src + (gl + W::G * m) * 16);
+            u.x2[m] = ld_stream16(src + (D / 2) * ES + (gl + W::G * m) * 16);
+        }
+    }
+}
+
+// Norm, RoPE and the stores of one unit.  Warp-uniform: every lane of the
+// warp calls it for the same unit (it synchronises the warp around csm).
+template <typename T, int D>
+__device__ __forceinline__ void process_unit(const QkDev& a, UnitRows<T, D>& u, int lane, int gl,
+                                             const uint4 (*wsm)[D * sizeof(T) / 16],
+                                             uint4* csm) {
+    using W = Wide<T, D>;
+    constexpr int G = W::G, C = W::C, NCH = W::NCH;
+    constexpr int64_t ES = sizeof(T);
+    constexpr int HALF = D / 2;
+    const int64_t t = u.t;
+    const int kind = u.kind, h = u.h;
+
+    if (__any_sync(0xffffffffu, kind < 2)) {  // some row of the unit needs cos/sin
+        __syncwarp();  // the previous unit's reads of csm are done
+        stage_cos_sin<T, D>(csm, a.cos ? a.cos + t * a.cs_st * ES : nullptr,
+                            a.cos ? a.sin + t * a.cs_st * ES : nullptr, a.inv_freq,
+                            a.cos ? 0.f : (float)load_index(a.pos, t, a.pos_type), lane);
+        __syncwarp();
+    }
+    int64_t blk = 0, slot = 0;
+    const bool slot_ok = a.store && kind >= 1 && kind <= 2 &&
+                         cache_slot(a, t, blk, slot, kind == 1 && h == 0 && gl == 0);
+
+    const bool has_w = kind == 0 ? a.qw != nullptr : a.kw != nullptr;
+    float ss = 0.f;
+    if (kind < 2 && has_w) {
+#pragma unroll
+        for (int m = 0; m < C; ++m) ss += sum_sq16<T>(u.x1[m]) + sum_sq16<T>(u.x2[m]);
+    }
+#pragma unroll
+    for (int o = G / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+
+    char* dst = nullptr;
+    char* dst2 = nullptr;
+    if (kind == 2) {  // V row: bit-exact copy into its page
+        if (slot_ok) dst = a.v_cache + (blk * a.c0 + (int64_t)h * a.c1 + slot * a.c2) * ES;
+    } else if (kind < 2) {
+        const float inv = has_w ? inv_rms_pow2<D>(ss, a.eps) : 1.f;
+        const uint4* w = wsm[kind];
+#pragma unroll
+        for (int m = 0; m < C; ++m) {
+            const int c = gl + G * m;
+            norm_rope_vec<T>(u.x1[m], u.x2[m], has_w, inv, w[c], w[NCH + c], csm[c],
+                             csm[NCH + c], csm[2 * NCH + c], csm[3 * NCH + c]);
+        }
+        if (kind == 0) {
+            dst = a.q_out + (t * a.qo_st + (int64_t)h * a.qo_sh) * ES;
+        } else {
+            if (a.k_out) dst2 = a.k_out + (t * a.ko_st + (int64_t)h * a.ko_sh) * ES;
+            if (slot_ok) dst = a.k_cache + (blk * a.c0 + (int64_t)h * a.c1 + slot * a.c2) * ES;
+        }
+    }
+    if (dst) {
+#pragma unroll
+        for (int m = 0; m < C; ++m) {
+            st16(dst + (gl + G * m) * 16, u.x1[m]);
+            st16(dst + HALF * ES + (gl + G * m) * 16, u.x2[m]);
+        }
+    }
+    if (dst2) {
+#pragma unroll
+        for (int m = 0; m < C; ++m) {
+            st16(dst2 + (gl + G * m) * 16, u.x1[m]);
+            st16(dst2 + HALF * ES + (gl + G * m) * 16, u.x2[m]);
+        }
+    }
+}
+
+// Grid-stride over units (measured on B200: issuing the next unit's loads
+// ahead of the current unit's arithmetic did not pay, the occupancy it costs
+// outweighs the extra bytes in flight).
+template <typename T, int D, typename IT>
+__global__ void __launch_bounds__(256, Wide<T, D>::C > 4 ? 2 : QF_QK_MIN_CTAS)
+    qk_norm_rope_wide_kernel(const QkDev a, const IT steps, const IT units) {
+    using W = Wide<T, D>;
+    constexpr int G = W::G, NCH = W::NCH;
+    constexpr int NV = 2 * NCH;  // 16-byte chunks per weight vector
+
+    __shared__ uint4 wsm[2][NV];        // q_norm and k_norm weights
+    __shared__ uint4 csm[8][4 * NCH];   // per warp: the current token's cos | sin rows
     for (int i = threadIdx.x; i < 2 * NV; i += blockDim.x) {
         const char* w = i < NV ? a.qw : a.kw;
         const int j = i < NV ? i : i - NV;
@@ -378,134 +520,35 @@ __global__ void __launch_bounds__(256, 3) qk_norm_rope_vec_kernel(const QkDev a)
     }
     __syncthreads();
 
-    const int lane = threadIdx.x & 31;
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int sub = lane / G;
     const int gl = lane - sub * G;
-    const int e0 = gl * EPV;
-    const int64_t off1 = e0 * ES, off2 = (HALF + e0) * ES;
-
-    const IT tpt = (IT)a.tasks_per_token;
-    const IT total = (IT)a.T * tpt;
     const IT warp = ((IT)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const IT nwarp = ((IT)gridDim.x * blockDim.x) >> 5;
-    const IT Hq = (IT)a.Hq, Hkv = (IT)a.Hkv;
-
-    for (IT base = warp * (HPW * U); base < total; base += nwarp * (HPW * U)) {
-        uint4 r1[U], r2[U];
-        int64_t tt[U], hh[U];
-        int kind[U];
-        bool act[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const IT task = base + (IT)(u * HPW + sub);
-            act[u] = task < total;
-            const IT t = act[u] ? task / tpt : 0;
-            const IT hx = act[u] ? task - t * tpt : 0;
-            tt[u] = (int64_t)t;
-            const char* src;
-            if (hx < Hq) {
-                kind[u] = 0;
-                hh[u] = (int64_t)hx;
-                src = a.q + (tt[u] * a.q_st + hh[u] * a.q_sh) * ES;
-            } else if (hx < Hq + Hkv) {
-                kind[u] = 1;
-                hh[u] = (int64_t)(hx - Hq);
-                src = a.k + (tt[u] * a.k_st + hh[u] * a.k_sh) * ES;
-            } else {
-                kind[u] = 2;
-                hh[u] = (int64_t)(hx - Hq - Hkv);
-                src = a.v + (tt[u] * a.v_st + hh[u] * a.v_sh) * ES;
-            }
-            if (act[u]) {
-                r1[u] = ld_stream16(src + off1);
-                r2[u] = ld_stream16(src + off2);
-            }
-        }
-
-        float ss[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            ss[u] = 0.f;
-            const bool has_w = kind[u] == 0 ? a.qw != nullptr : a.kw != nullptr;
-            if (act[u] && kind[u] < 2 && has_w) ss[u] = sum_sq16<T>(r1[u]) + sum_sq16<T>(r2[u]);
-        }
-        // every lane runs every shuffle: the G-lane groups reduce side by side
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-#pragma unroll
-            for (int o = G / 2; o > 0; o >>= 1) ss[u] += __shfl_xor_sync(0xffffffffu, ss[u], o);
-        }
-
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            if (!act[u]) continue;
-            const int64_t t = tt[u], h = hh[u];
-            if (kind[u] == 2) {  // V row: bit-exact copy into its page
-                int64_t blk, slot;
-                if (cache_slot(a, t, blk, slot, gl == 0 && h == 0)) {
-                    char* dst = a.v_cache + (blk * a.c0 + h * a.c1 + slot * a.c2) * ES;
-                    st16(dst + off1, r1[u]);
-                    st16(dst + off2, r2[u]);
-                }
-                continue;
-            }
-            const bool is_q = kind[u] == 0;
-            const bool has_w = is_q ? a.qw != nullptr : a.kw != nullptr;
-            const float inv = has_w ? inv_rms(ss[u], D, a.eps) : 1.f;
-            uint4 c1, c2, s1, s2;
-            if (a.cos) {
-                const char* cr = a.cos + t * a.cs_st * ES;
-                const char* sr = a.sin + t * a.cs_st * ES;
-                c1 = ld_shared_ro16(cr + off1);
-                c2 = ld_shared_ro16(cr + off2);
-                s1 = ld_shared_ro16(sr + off1);
-                s2 = ld_shared_ro16(sr + off2);
-            } else {
-                cos_sin_vec<T>(a.inv_freq, e0, (float)load_index(a.pos, t, a.pos_type), c1, s1);
-                c2 = c1;
-                s2 = s1;
-            }
-            const uint4* w = wsm[is_q ? 0 : 1];
-            norm_rope_vec<T>(r1[u], r2[u], has_w, inv, w[gl], w[NV / 2 + gl], c1, c2, s1, s2);
-            if (is_q) {
-                char* dst = a.q_out + (t * a.qo_st + h * a.qo_sh) * ES;
-                st16(dst + off1, r1[u]);
-                st16(dst + off2, r2[u]);
-            } else {
-                if (a.k_out) {
-                    char* dst = a.k_out + (t * a.ko_st + h * a.ko_sh) * ES;
-                    st16(dst + off1, r1[u]);
-                    st16(dst + off2, r2[u]);
-                }
-                int64_t blk, slot;
-                if (a.store && cache_slot(a, t, blk, slot, gl == 0 && h == 0)) {
-                    char* dst = a.k_cache + (blk * a.c0 + h * a.c1 + slot * a.c2) * ES;
-                    st16(dst + off1, r1[u]);
-                    st16(dst + off2, r2[u]);
-                }
-            }
-        }
+    for (IT unit = warp; unit < units; unit += nwarp) {
+        UnitRows<T, D> u;
+        load_unit<T, D, IT>(a, unit, steps, sub, gl, u);
+        process_unit<T, D>(a, u, lane, gl, wsm, csm[wib]);
     }
 }
 
 template <typename T, int D, typename IT>
-int launch_qk_vec_it(const QkDev& a, cudaStream_t stream) {
-    using R = VecRow<T, D>;
-    constexpr auto kernel = qk_norm_rope_vec_kernel<T, D, IT>;
+int launch_qk_wide_it(const QkDev& a, int64_t steps, int64_t units, cudaStream_t stream) {
+    constexpr auto kernel = qk_norm_rope_wide_kernel<T, D, IT>;
     const int threads = 256;
-    const int64_t total = a.T * a.tasks_per_token;
-    const int64_t warps = ceil_div(total, (int64_t)R::HPW * R::U);
-    const int64_t need = ceil_div(warps, threads / 32);
+    const int64_t need = ceil_div(units, threads / 32);
     const int64_t fill = (int64_t)sm_count() * resident_ctas<kernel>(threads);
-    kernel<<<(unsigned)std::min<int64_t>(need, fill), threads, 0, stream>>>(a);
+    kernel<<<(unsigned)std::min<int64_t>(need, fill), threads, 0, stream>>>(a, (IT)steps,
+                                                                           (IT)units);
     return check_launch();
 }
 
 template <typename T, int D>
-int launch_qk_vec(const QkDev& a, cudaStream_t stream) {
-    if (a.T * a.tasks_per_token < (int64_t(1) << 31))
-        return launch_qk_vec_it<T, D, uint32_t>(a, stream);
-    return launch_qk_vec_it<T, D, uint64_t>(a, stream);
+int launch_qk_wide(const QkDev& a, cudaStream_t stream) {
+    const int64_t steps = ceil_div(a.tasks_per_token, (int64_t)Wide<T, D>::HPW);
+    const int64_t units = a.T * steps;
+    if (units < (int64_t(1) << 31)) return launch_qk_wide_it<T, D, uint32_t>(a, steps, units, stream);
+    return launch_qk_wide_it<T, D, uint64_t>(a, steps, units, stream);
 }
 
 template <typename T, int D>
@@ -522,12 +565,17 @@ int launch_qk(const QkDev& a, cudaStream_t stream) {
     return check_launch();
 }
 
+template <typename T, int D>
+int launch_qk_best(const QkDev& a, bool vec, cudaStream_t stream) {
+    return vec ? launch_qk_wide<T, D>(a, stream) : launch_qk<T, D>(a, stream);
+}
+
 template <typename T>
 int dispatch_qk(const QkDev& a, int64_t D, bool vec, cudaStream_t stream) {
     switch (D) {
-    case 64: return vec ? launch_qk_vec<T, 64>(a, stream) : launch_qk<T, 64>(a, stream);
-    case 128: return vec ? launch_qk_vec<T, 128>(a, stream) : launch_qk<T, 128>(a, stream);
-    case 256: return vec ? launch_qk_vec<T, 256>(a, stream) : launch_qk<T, 256>(a, stream);
+    case 64: return launch_qk_best<T, 64>(a, vec, stream);
+    case 128: return launch_qk_best<T, 128>(a, vec, stream);
+    case 256: return launch_qk_best<T, 256>(a, vec, stream);
     default: return QF_ERR_UNSUPPORTED;
     }
 }
