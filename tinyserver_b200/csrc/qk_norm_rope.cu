@@ -297,14 +297,18 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const QkDev a) {
 //    the cache slot) is set up once per unit and shared by HPW rows.
 // For 16-bit types the norm's weight multiply and all of RoPE run as packed
 // .rn ops (see Packed), which round exactly where torch's separate kernels do.
-// Lanes per head row and the CTAs per SM the register budget is sized for
-// (compile-time knobs; the defaults are the best of a sweep on B200 at
-// Qwen3-8B shapes: 2, 4 and 8 lanes per row, with and without prefetching).
+// Lanes per head row, CTAs per SM the register budget is sized for, and warp
+// steps per work unit (compile-time knobs; the defaults are the best of
+// sweeps on B200 at Qwen3-8B shapes: 2/4/8 lanes per row, 1/2/3/6 steps per
+// unit, with and without prefetching the next unit).
 #ifndef QF_QK_LANES
 #define QF_QK_LANES 4
 #endif
 #ifndef QF_QK_MIN_CTAS
 #define QF_QK_MIN_CTAS 3
+#endif
+#ifndef QF_QK_STEPS
+#define QF_QK_STEPS 2  // warp steps (HPW head rows each) per work unit
 #endif
 
 template <typename T, int D>
@@ -400,67 +404,54 @@ __device__ __forceinline__ void stage_cos_sin(uint4* cs, const char* cos_row,
     }
 }
 
-// One unit's rows in registers, and where they came from.
+// One warp step's rows in registers (HPW head rows of one token), and what
+// they are.
 template <typename T, int D>
-struct UnitRows {
+struct StepRows {
     uint4 x1[Wide<T, D>::C], x2[Wide<T, D>::C];
-    int64_t t;
     int kind;  // 0 q, 1 k, 2 v, 3 past the last row
-    int h;
+    int h;     // head index within its kind
 };
 
-template <typename T, int D, typename IT>
-__device__ __forceinline__ void load_unit(const QkDev& a, IT unit, IT steps, int sub, int gl,
-                                          UnitRows<T, D>& u) {
+template <typename T, int D>
+__device__ __forceinline__ void load_step(const QkDev& a, int64_t t, int step, int sub, int gl,
+                                          StepRows<T, D>& r) {
     using W = Wide<T, D>;
     constexpr int64_t ES = sizeof(T);
-    const IT tu = unit / steps;
-    u.t = (int64_t)tu;
-    const int row = (int)(unit - tu * steps) * W::HPW + sub;
+    const int row = step * W::HPW + sub;
     const int Hq = (int)a.Hq, Hkv = (int)a.Hkv;
-    u.kind = row < Hq ? 0 : row < Hq + Hkv ? 1 : row < (int)a.tasks_per_token ? 2 : 3;
-    u.h = u.kind == 0 ? row : u.kind == 1 ? row - Hq : row - Hq - Hkv;
-    const char* src = u.kind == 0   ? a.q + (u.t * a.q_st + (int64_t)u.h * a.q_sh) * ES
-                      : u.kind == 1 ? a.k + (u.t * a.k_st + (int64_t)u.h * a.k_sh) * ES
-                                    : a.v + (u.t * a.v_st + (int64_t)u.h * a.v_sh) * ES;
-    if (u.kind < 3) {
+    r.kind = row < Hq ? 0 : row < Hq + Hkv ? 1 : row < (int)a.tasks_per_token ? 2 : 3;
+    r.h = r.kind == 0 ? row : r.kind == 1 ? row - Hq : row - Hq - Hkv;
+    const char* src = r.kind == 0   ? a.q + (t * a.q_st + (int64_t)r.h * a.q_sh) * ES
+                      : r.kind == 1 ? a.k + (t * a.k_st + (int64_t)r.h * a.k_sh) * ES
+                                    : a.v + (t * a.v_st + (int64_t)r.h * a.v_sh) * ES;
+    if (r.kind < 3) {
 #pragma unroll
         for (int m = 0; m < W::C; ++m) {
-            u.x1[m] = ld_stream16(src + (gl + W::G * m) * 16);
-            u.x2[m] = ld_stream16(src + (D / 2) * ES + (gl + W::G * m) * 16);
+            r.x1[m] = ld_stream16(src + (gl + W::G * m) * 16);
+            r.x2[m] = ld_stream16(src + (D / 2) * ES + (gl + W::G * m) * 16);
         }
     }
 }
 
-// Norm, RoPE and the stores of one unit.  Warp-uniform: every lane of the
-// warp calls it for the same unit (it synchronises the warp around csm).
+// Norm, RoPE and the stores of one warp step; csm holds the token's cos/sin
+// rows and cache_off the byte offset of its (block, head 0, slot) page row.
 template <typename T, int D>
-__device__ __forceinline__ void process_unit(const QkDev& a, UnitRows<T, D>& u, int lane, int gl,
-                                             const uint4 (*wsm)[D * sizeof(T) / 16],
-                                             uint4* csm) {
+__device__ __forceinline__ void process_step(const QkDev& a, int64_t t, StepRows<T, D>& r,
+                                             int gl, const uint4 (*wsm)[D * sizeof(T) / 16],
+                                             const uint4* csm, bool slot_ok,
+                                             int64_t cache_off) {
     using W = Wide<T, D>;
     constexpr int G = W::G, C = W::C, NCH = W::NCH;
     constexpr int64_t ES = sizeof(T);
     constexpr int HALF = D / 2;
-    const int64_t t = u.t;
-    const int kind = u.kind, h = u.h;
-
-    if (__any_sync(0xffffffffu, kind < 2)) {  // some row of the unit needs cos/sin
-        __syncwarp();  // the previous unit's reads of csm are done
-        stage_cos_sin<T, D>(csm, a.cos ? a.cos + t * a.cs_st * ES : nullptr,
-                            a.cos ? a.sin + t * a.cs_st * ES : nullptr, a.inv_freq,
-                            a.cos ? 0.f : (float)load_index(a.pos, t, a.pos_type), lane);
-        __syncwarp();
-    }
-    int64_t blk = 0, slot = 0;
-    const bool slot_ok = a.store && kind >= 1 && kind <= 2 &&
-                         cache_slot(a, t, blk, slot, kind == 1 && h == 0 && gl == 0);
+    const int kind = r.kind, h = r.h;
 
     const bool has_w = kind == 0 ? a.qw != nullptr : a.kw != nullptr;
     float ss = 0.f;
     if (kind < 2 && has_w) {
 #pragma unroll
-        for (int m = 0; m < C; ++m) ss += sum_sq16<T>(u.x1[m]) + sum_sq16<T>(u.x2[m]);
+        for (int m = 0; m < C; ++m) ss += sum_sq16<T>(r.x1[m]) + sum_sq16<T>(r.x2[m]);
     }
 #pragma unroll
     for (int o = G / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -468,48 +459,52 @@ __device__ __forceinline__ void process_unit(const QkDev& a, UnitRows<T, D>& u, 
     char* dst = nullptr;
     char* dst2 = nullptr;
     if (kind == 2) {  // V row: bit-exact copy into its page
-        if (slot_ok) dst = a.v_cache + (blk * a.c0 + (int64_t)h * a.c1 + slot * a.c2) * ES;
+        if (slot_ok) dst = a.v_cache + cache_off + (int64_t)h * a.c1 * ES;
     } else if (kind < 2) {
         const float inv = has_w ? inv_rms_pow2<D>(ss, a.eps) : 1.f;
         const uint4* w = wsm[kind];
 #pragma unroll
         for (int m = 0; m < C; ++m) {
             const int c = gl + G * m;
-            norm_rope_vec<T>(u.x1[m], u.x2[m], has_w, inv, w[c], w[NCH + c], csm[c],
+            norm_rope_vec<T>(r.x1[m], r.x2[m], has_w, inv, w[c], w[NCH + c], csm[c],
                              csm[NCH + c], csm[2 * NCH + c], csm[3 * NCH + c]);
         }
         if (kind == 0) {
             dst = a.q_out + (t * a.qo_st + (int64_t)h * a.qo_sh) * ES;
         } else {
             if (a.k_out) dst2 = a.k_out + (t * a.ko_st + (int64_t)h * a.ko_sh) * ES;
-            if (slot_ok) dst = a.k_cache + (blk * a.c0 + (int64_t)h * a.c1 + slot * a.c2) * ES;
+            if (slot_ok) dst = a.k_cache + cache_off + (int64_t)h * a.c1 * ES;
         }
     }
     if (dst) {
 #pragma unroll
         for (int m = 0; m < C; ++m) {
-            st16(dst + (gl + G * m) * 16, u.x1[m]);
-            st16(dst + HALF * ES + (gl + G * m) * 16, u.x2[m]);
+            st16(dst + (gl + G * m) * 16, r.x1[m]);
+            st16(dst + HALF * ES + (gl + G * m) * 16, r.x2[m]);
         }
     }
     if (dst2) {
 #pragma unroll
         for (int m = 0; m < C; ++m) {
-            st16(dst2 + (gl + G * m) * 16, u.x1[m]);
-            st16(dst2 + HALF * ES + (gl + G * m) * 16, u.x2[m]);
+            st16(dst2 + (gl + G * m) * 16, r.x1[m]);
+            st16(dst2 + HALF * ES + (gl + G * m) * 16, r.x2[m]);
         }
     }
 }
 
-// Grid-stride over units (measured on B200: issuing the next unit's loads
-// ahead of the current unit's arithmetic did not pay, the occupancy it costs
-// outweighs the extra bytes in flight).
+// Grid-stride over units of U warp steps of one token.  A unit issues the
+// loads of all its steps first, then does the per-token work once (the
+// position and cache-slot lookups, the cos/sin staging), then runs the steps'
+// independent arithmetic back to back, which gives the scheduler U chains to
+// interleave.
 template <typename T, int D, typename IT>
 __global__ void __launch_bounds__(256, Wide<T, D>::C > 4 ? 2 : QF_QK_MIN_CTAS)
-    qk_norm_rope_wide_kernel(const QkDev a, const IT steps, const IT units) {
+    qk_norm_rope_wide_kernel(const QkDev a, const IT steps, const IT upt, const IT units) {
     using W = Wide<T, D>;
-    constexpr int G = W::G, NCH = W::NCH;
+    constexpr int G = W::G, NCH = W::NCH, HPW = W::HPW;
+    constexpr int U = QF_QK_STEPS;
     constexpr int NV = 2 * NCH;  // 16-byte chunks per weight vector
+    constexpr int64_t ES = sizeof(T);
 
     __shared__ uint4 wsm[2][NV];        // q_norm and k_norm weights
     __shared__ uint4 csm[8][4 * NCH];   // per warp: the current token's cos | sin rows
@@ -523,32 +518,62 @@ __global__ void __launch_bounds__(256, Wide<T, D>::C > 4 ? 2 : QF_QK_MIN_CTAS)
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int sub = lane / G;
     const int gl = lane - sub * G;
+    const int Hq = (int)a.Hq;
     const IT warp = ((IT)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const IT nwarp = ((IT)gridDim.x * blockDim.x) >> 5;
     for (IT unit = warp; unit < units; unit += nwarp) {
-        UnitRows<T, D> u;
-        load_unit<T, D, IT>(a, unit, steps, sub, gl, u);
-        process_unit<T, D>(a, u, lane, gl, wsm, csm[wib]);
+        const IT tu = unit / upt;
+        const int64_t t = (int64_t)tu;
+        const int s0 = (int)(unit - tu * upt) * U;
+        const int row0 = s0 * HPW, row_end = (s0 + U) * HPW;  // this unit's row range
+
+        // per-token index loads first: they complete under the row loads
+        const bool rope = row0 < Hq + (int)a.Hkv;
+        const float pos = rope && !a.cos ? (float)load_index(a.pos, t, a.pos_type) : 0.f;
+        int64_t blk = 0, slot = 0;
+        const bool slot_ok = a.store && row_end > Hq &&
+                             cache_slot(a, t, blk, slot, lane == 0 && row0 <= Hq);
+        const int64_t cache_off = (blk * a.c0 + slot * a.c2) * ES;
+
+        StepRows<T, D> r[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            if (s0 + u < (int)steps) load_step<T, D>(a, t, s0 + u, sub, gl, r[u]);
+            else r[u].kind = 3;
+        }
+        if (rope) {
+            __syncwarp();  // the previous unit's reads of csm are done
+            stage_cos_sin<T, D>(csm[wib], a.cos ? a.cos + t * a.cs_st * ES : nullptr,
+                                a.cos ? a.sin + t * a.cs_st * ES : nullptr, a.inv_freq, pos,
+                                lane);
+            __syncwarp();
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            process_step<T, D>(a, t, r[u], gl, wsm, csm[wib], slot_ok, cache_off);
     }
 }
 
 template <typename T, int D, typename IT>
-int launch_qk_wide_it(const QkDev& a, int64_t steps, int64_t units, cudaStream_t stream) {
+int launch_qk_wide_it(const QkDev& a, int64_t steps, int64_t upt, int64_t units,
+                      cudaStream_t stream) {
     constexpr auto kernel = qk_norm_rope_wide_kernel<T, D, IT>;
     const int threads = 256;
     const int64_t need = ceil_div(units, threads / 32);
     const int64_t fill = (int64_t)sm_count() * resident_ctas<kernel>(threads);
-    kernel<<<(unsigned)std::min<int64_t>(need, fill), threads, 0, stream>>>(a, (IT)steps,
-                                                                           (IT)units);
+    kernel<<<(unsigned)std::min<int64_t>(need, fill), threads, 0, stream>>>(
+        a, (IT)steps, (IT)upt, (IT)units);
     return check_launch();
 }
 
 template <typename T, int D>
 int launch_qk_wide(const QkDev& a, cudaStream_t stream) {
     const int64_t steps = ceil_div(a.tasks_per_token, (int64_t)Wide<T, D>::HPW);
-    const int64_t units = a.T * steps;
-    if (units < (int64_t(1) << 31)) return launch_qk_wide_it<T, D, uint32_t>(a, steps, units, stream);
-    return launch_qk_wide_it<T, D, uint64_t>(a, steps, units, stream);
+    const int64_t upt = ceil_div(steps, (int64_t)QF_QK_STEPS);  // units per token
+    const int64_t units = a.T * upt;
+    if (units < (int64_t(1) << 31))
+        return launch_qk_wide_it<T, D, uint32_t>(a, steps, upt, units, stream);
+    return launch_qk_wide_it<T, D, uint64_t>(a, steps, upt, units, stream);
 }
 
 template <typename T, int D>
