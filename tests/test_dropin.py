@@ -43,6 +43,9 @@ def test_paged_install_rebinds_attention():
                               device="cpu")
     patches.install_fused(model, context=lambda: None, attention=object())
     assert all("forward" in layer.self_attn.__dict__ for layer in model.model.layers)
+    assert "forward" in model.model.__dict__  # the fused layer loop
+    with pytest.raises(ValueError, match="use_cache=False"):
+        model.model(input_ids=torch.zeros(1, 4, dtype=torch.long), use_cache=True)
     k0 = model.model.layers[0].self_attn.k_cache
     assert k0.shape == (8, model.config.num_key_value_heads, 16, model.config.head_dim)
 

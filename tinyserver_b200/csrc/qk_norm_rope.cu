@@ -521,6 +521,7 @@ __global__ void __launch_bounds__(256, Wide<T, D>::C > 4 ? 2 : QF_QK_MIN_CTAS)
     const int Hq = (int)a.Hq;
     const IT warp = ((IT)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const IT nwarp = ((IT)gridDim.x * blockDim.x) >> 5;
+    int64_t staged = -1;  // token whose cos/sin rows csm[wib] holds
     for (IT unit = warp; unit < units; unit += nwarp) {
         const IT tu = unit / upt;
         const int64_t t = (int64_t)tu;
@@ -529,7 +530,8 @@ __global__ void __launch_bounds__(256, Wide<T, D>::C > 4 ? 2 : QF_QK_MIN_CTAS)
 
         // per-token index loads first: they complete under the row loads
         const bool rope = row0 < Hq + (int)a.Hkv;
-        const float pos = rope && !a.cos ? (float)load_index(a.pos, t, a.pos_type) : 0.f;
+        const float pos = rope && !a.cos && t != staged ? (float)load_index(a.pos, t, a.pos_type)
+                                                        : 0.f;
         int64_t blk = 0, slot = 0;
         const bool slot_ok = a.store && row_end > Hq &&
                              cache_slot(a, t, blk, slot, lane == 0 && row0 <= Hq);
@@ -541,12 +543,13 @@ __global__ void __launch_bounds__(256, Wide<T, D>::C > 4 ? 2 : QF_QK_MIN_CTAS)
             if (s0 + u < (int)steps) load_step<T, D>(a, t, s0 + u, sub, gl, r[u]);
             else r[u].kind = 3;
         }
-        if (rope) {
+        if (rope && t != staged) {
             __syncwarp();  // the previous unit's reads of csm are done
             stage_cos_sin<T, D>(csm[wib], a.cos ? a.cos + t * a.cs_st * ES : nullptr,
                                 a.cos ? a.sin + t * a.cs_st * ES : nullptr, a.inv_freq, pos,
                                 lane);
             __syncwarp();
+            staged = t;
         }
 #pragma unroll
         for (int u = 0; u < U; ++u)

@@ -12,6 +12,12 @@
 // reference op by op: h = rnd(res + x); y = rnd(w * rnd(h * rsqrt(var + eps))).
 #include "qf_common.cuh"
 
+// Threads per row for rows up to 4 * QF_RMS_MAX_THREADS 16-byte vectors
+// (compile-time knob; rows are split into 1, 2 or 4 vectors per thread).
+#ifndef QF_RMS_MAX_THREADS
+#define QF_RMS_MAX_THREADS 256
+#endif
+
 namespace qf {
 namespace {
 
@@ -51,7 +57,7 @@ __device__ __forceinline__ float inv_rms(float sum_sq, int64_t H, float eps) {
 // scale with packed .rn ops (see Packed): the same roundings as torch's
 // separate add, cast and mul kernels.
 template <typename T, int VPT, bool ADD>
-__global__ void __launch_bounds__(VPT == 8 ? 512 : 256) rmsnorm_vec_kernel(const NormArgs a) {
+__global__ void __launch_bounds__(VPT == 8 ? 512 : QF_RMS_MAX_THREADS) rmsnorm_vec_kernel(const NormArgs a) {
     __shared__ float red[2][32];
     const int tid = threadIdx.x;
     const int nthr = blockDim.x;
@@ -148,7 +154,7 @@ __global__ void __launch_bounds__(256) rmsnorm_scalar_kernel(const NormArgs a) {
 
 template <typename T, int VPT, bool ADD>
 int launch_vec(const NormArgs& a, cudaStream_t stream) {
-    const int threads = (int)std::min<int64_t>(VPT == 8 ? 512 : 256,
+    const int threads = (int)std::min<int64_t>(VPT == 8 ? 512 : QF_RMS_MAX_THREADS,
                                                ceil_div(ceil_div(a.nvec, VPT), 32) * 32);
     const int per_sm = resident_ctas<rmsnorm_vec_kernel<T, VPT, ADD>>(threads);
     const int64_t grid = std::min<int64_t>(a.rows, (int64_t)sm_count() * per_sm);
@@ -168,9 +174,9 @@ int dispatch(NormArgs& a, cudaStream_t stream) {
     if (vec) {
         a.nvec = a.H / EPV;
         // at most 256 threads per row where possible: more rows in flight per SM
-        if (a.nvec <= 256) return launch_vec<T, 1, ADD>(a, stream);
-        if (a.nvec <= 512) return launch_vec<T, 2, ADD>(a, stream);
-        if (a.nvec <= 1024) return launch_vec<T, 4, ADD>(a, stream);
+        if (a.nvec <= QF_RMS_MAX_THREADS) return launch_vec<T, 1, ADD>(a, stream);
+        if (a.nvec <= 2 * QF_RMS_MAX_THREADS) return launch_vec<T, 2, ADD>(a, stream);
+        if (a.nvec <= 4 * QF_RMS_MAX_THREADS) return launch_vec<T, 4, ADD>(a, stream);
         if (a.nvec <= 4096) return launch_vec<T, 8, ADD>(a, stream);
     }
     if (a.rows > 0x7fffffffLL) return QF_ERR_UNSUPPORTED;

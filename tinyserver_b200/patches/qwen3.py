@@ -11,7 +11,9 @@ scheduler call into libqwen3fused without a change:
 * every ``Qwen3RMSNorm.forward(hidden_states)`` (input/post-attention/final
   norms and the per-head q_norm/k_norm)        -> :func:`~tinyserver_b200.rms_norm`
 * ``Qwen3DecoderLayer.forward(...)``: the post-attention residual add and
-  ``post_attention_layernorm`` become one :func:`~tinyserver_b200.fused_add_rms_norm`
+  ``post_attention_layernorm`` become one :func:`~tinyserver_b200.fused_add_rms_norm`;
+  on a paged model ``Qwen3Model.forward`` also fuses each end-of-layer add
+  into the next layer's input norm (or the final norm)
 * ``Qwen3MLP.forward(x)``: ``act_fn(gate) * up`` -> :func:`~tinyserver_b200.silu_and_mul`
 * on a paged model (one the reference's cache allocator gave ``k_cache`` /
   ``v_cache``): the attention pre-processing of the reference's patched
@@ -95,6 +97,54 @@ def _decoder_layer_forward(layer: torch.nn.Module) -> Callable[..., torch.Tensor
                                                        post.variance_epsilon)
         hidden_states = layer.mlp(hidden_states)
         return residual + hidden_states
+
+    return forward
+
+
+def _model_forward(base: torch.nn.Module) -> Callable[..., Any]:
+    """Qwen3Model.forward (modeling_qwen3.py:378-437) for the paged serving path,
+    with every residual add fused into the norm that follows it: the
+    post-attention add into post_attention_layernorm, and the end-of-layer add
+    (HF:333) into the NEXT layer's input_layernorm, or into the final norm
+    after the last layer.  That removes one full read and write of the hidden
+    state per layer against running the decoder layers one by one.  The
+    causal masks are not built: the paged attention, like the reference's
+    (qwen3.py:216-418), never reads them."""
+    from transformers.modeling_outputs import BaseModelOutputWithPast
+
+    layers = list(base.layers[: base.config.num_hidden_layers])
+
+    def forward(input_ids: torch.Tensor | None = None, attention_mask: Any = None,
+                position_ids: torch.Tensor | None = None, past_key_values: Any = None,
+                inputs_embeds: torch.Tensor | None = None, use_cache: bool | None = None,
+                **kwargs: Any):
+        if (input_ids is None) ^ (inputs_embeds is not None):
+            raise ValueError("You must specify exactly one of input_ids or inputs_embeds")
+        if use_cache or past_key_values is not None:
+            raise ValueError("the fused paged model keeps its own paged KV cache: call it "
+                             "with use_cache=False and no past_key_values")
+        hidden = base.embed_tokens(input_ids) if inputs_embeds is None else inputs_embeds
+        if position_ids is None:
+            position_ids = torch.arange(hidden.shape[1], device=hidden.device).unsqueeze(0)
+        position_embeddings = base.rotary_emb(hidden, position_ids)
+        residual = hidden
+        first = layers[0].input_layernorm
+        x = F.rms_norm(hidden, first.weight, first.variance_epsilon)
+        own = False  # residual is a buffer of ours (never the caller's inputs_embeds)
+        for i, layer in enumerate(layers):
+            x, _ = layer.self_attn(hidden_states=x, attention_mask=None,
+                                   position_ids=position_ids, past_key_values=None,
+                                   use_cache=False, position_embeddings=position_embeddings,
+                                   **kwargs)
+            post = layer.post_attention_layernorm
+            x, residual = F.fused_add_rms_norm(x, residual, post.weight, post.variance_epsilon,
+                                               inplace=own)
+            own = True
+            x = layer.mlp(x)
+            nxt = layers[i + 1].input_layernorm if i + 1 < len(layers) else base.norm
+            x, residual = F.fused_add_rms_norm(x, residual, nxt.weight, nxt.variance_epsilon,
+                                               inplace=True)
+        return BaseModelOutputWithPast(last_hidden_state=x, past_key_values=None)
 
     return forward
 
@@ -293,6 +343,7 @@ def install_fused(model: torch.nn.Module, *, paged: bool | None = None,
                                  "(allocate the cache first)")
             attn._tinyserver_b200_inv_freq = inv_freq
             attn.forward = _paged_attention_forward(attn, ctx, backend)
+        base.forward = _model_forward(base)
     return model
 
 
