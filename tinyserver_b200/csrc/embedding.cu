@@ -23,6 +23,8 @@ struct EmbArgs {
 template <int VPT>
 __global__ void __launch_bounds__(256) embedding_vec_kernel(const EmbArgs a, const int64_t nvec,
                                                             const int64_t chunks) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t row = blockIdx.x / chunks;
     const int64_t chunk = blockIdx.x - row * chunks;
     const int64_t id = load_index(a.ids, row, a.index_type);
@@ -84,8 +86,8 @@ extern "C" int qf_embedding(const void* ids, int index_type, const void* table, 
         const int64_t chunks = qf::ceil_div(nvec, (int64_t)threads * VPT);
         const int64_t blocks = num_tokens * chunks;
         if (blocks <= 0x7fffffffLL) {
-            qf::embedding_vec_kernel<VPT><<<(unsigned)blocks, threads, 0, stream>>>(a, nvec, chunks);
-            return qf::check_launch();
+            return qf::launch_pdl(qf::embedding_vec_kernel<VPT>, (unsigned)blocks, threads, 0,
+                                  stream, a, nvec, chunks);
         }
     }
     const int64_t blocks =

@@ -273,6 +273,31 @@ __device__ __forceinline__ void flag(int32_t* status, int32_t bits) {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch (sm_90+).  The hot-path kernels are launched
+// with programmatic stream serialization: the next kernel in the stream may be
+// launched -- its CTAs scheduled onto SMs as the previous kernel's retire --
+// before the previous one has finished.  Every kernel launched that way calls
+// pdl_wait() before its first global memory access, which blocks until the
+// preceding grid has completed and its writes are visible, so the overlap is
+// only launch latency and CTA rasterisation, never data.  pdl_trigger()
+// allows the following grid to begin launching.
+#ifndef QF_PDL
+#define QF_PDL 1
+#endif
+
+__device__ __forceinline__ void pdl_wait() {
+#if QF_PDL
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+}
+
+__device__ __forceinline__ void pdl_trigger() {
+#if QF_PDL
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+#endif
+}
+
+// ---------------------------------------------------------------------------
 // Host side.
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -285,6 +310,25 @@ int launch_failed(cudaError_t e);
 // Check the launch that was just issued.
 inline int check_launch() {
     cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? QF_OK : launch_failed(e);
+}
+
+// Launch a kernel that calls pdl_wait() before touching global memory, with
+// programmatic stream serialization (see pdl_wait).
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem,
+               cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = QF_PDL;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
     return e == cudaSuccess ? QF_OK : launch_failed(e);
 }
 

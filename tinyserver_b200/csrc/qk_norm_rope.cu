@@ -508,6 +508,8 @@ __global__ void __launch_bounds__(256, Wide<T, D>::C > 4 ? 2 : QF_QK_MIN_CTAS)
 
     __shared__ uint4 wsm[2][NV];        // q_norm and k_norm weights
     __shared__ uint4 csm[8][4 * NCH];   // per warp: the current token's cos | sin rows
+    pdl_wait();
+    pdl_trigger();
     for (int i = threadIdx.x; i < 2 * NV; i += blockDim.x) {
         const char* w = i < NV ? a.qw : a.kw;
         const int j = i < NV ? i : i - NV;
@@ -564,9 +566,8 @@ int launch_qk_wide_it(const QkDev& a, int64_t steps, int64_t upt, int64_t units,
     const int threads = 256;
     const int64_t need = ceil_div(units, threads / 32);
     const int64_t fill = (int64_t)sm_count() * resident_ctas<kernel>(threads);
-    kernel<<<(unsigned)std::min<int64_t>(need, fill), threads, 0, stream>>>(
-        a, (IT)steps, (IT)upt, (IT)units);
-    return check_launch();
+    return launch_pdl(kernel, (unsigned)std::min<int64_t>(need, fill), threads, 0, stream, a,
+                      (IT)steps, (IT)upt, (IT)units);
 }
 
 template <typename T, int D>

@@ -63,6 +63,8 @@ __global__ void __launch_bounds__(VPT == 8 ? 512 : QF_RMS_MAX_THREADS) rmsnorm_v
     const int nthr = blockDim.x;
     const int lane = tid & 31, warp = tid >> 5, nwarps = nthr >> 5;
     constexpr int64_t ES = sizeof(T);
+    pdl_wait();
+    pdl_trigger();
 
     uint4 w[VPT];
 #pragma unroll
@@ -158,8 +160,7 @@ int launch_vec(const NormArgs& a, cudaStream_t stream) {
                                                ceil_div(ceil_div(a.nvec, VPT), 32) * 32);
     const int per_sm = resident_ctas<rmsnorm_vec_kernel<T, VPT, ADD>>(threads);
     const int64_t grid = std::min<int64_t>(a.rows, (int64_t)sm_count() * per_sm);
-    rmsnorm_vec_kernel<T, VPT, ADD><<<(unsigned)grid, threads, 0, stream>>>(a);
-    return check_launch();
+    return launch_pdl(rmsnorm_vec_kernel<T, VPT, ADD>, (unsigned)grid, threads, 0, stream, a);
 }
 
 template <typename T, bool ADD>

@@ -58,6 +58,8 @@ __device__ __forceinline__ uint4 silu_mul16(const uint4& g, const uint4& u) {
 template <typename T, int VPT>
 __global__ void __launch_bounds__(256) silu_mul_vec_kernel(const SiluArgs a, const int64_t nvec,
                                                            const int64_t chunks) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t row = blockIdx.x / chunks;
     const int64_t chunk = blockIdx.x - row * chunks;
     const char* g = a.gate + row * a.gs * (int64_t)sizeof(T);
@@ -107,8 +109,8 @@ int dispatch(const SiluArgs& a, cudaStream_t stream) {
         const int64_t chunks = ceil_div(nvec, (int64_t)threads * VPT);
         const int64_t blocks = a.rows * chunks;
         if (blocks <= 0x7fffffffLL) {
-            silu_mul_vec_kernel<T, VPT><<<(unsigned)blocks, threads, 0, stream>>>(a, nvec, chunks);
-            return check_launch();
+            return launch_pdl(silu_mul_vec_kernel<T, VPT>, (unsigned)blocks, threads, 0, stream,
+                              a, nvec, chunks);
         }
     }
     const int64_t blocks =
