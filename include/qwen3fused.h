@@ -200,6 +200,46 @@ int qf_build_slot_mapping(const int32_t* cu_seqlens, int64_t num_seqs,
                           int32_t* status, cudaStream_t stream);
 
 /* ---------------------------------------------------------------------- */
+/* Decode paged attention: one query token per sequence against its cached
+ * tokens.  Replaces paged_attention_forward (server/model/kernels/
+ * paged_attention.py:124-192; Triton kernel :8-121):
+ *   out[s, h, :] = softmax(q[s, h] . K_s^T * scale) @ V_s      (fp32 math)
+ * where token j < seq_lens[s] of sequence s sits at
+ * cache[block_tables[s, j / block_size], h / (Hq / Hkv), j % block_size, :].
+ * q, out: (num_seqs, Hq, head_dim) with sequence/head strides, head_dim
+ * contiguous; caches (N, Hkv, B, D) with strides (head_dim contiguous, rows
+ * 16-byte aligned); block_tables: int32 rows; seq_lens: int32.
+ * head_dim 64/128/256; Hq / Hkv in {1, 2, 4, 8}.
+ * workspace: fp32 scratch that lets one sequence be split over several CTAs;
+ * pass at least qf_paged_attention_workspace_bytes(...) bytes for the
+ * longest sequence the block tables allow (max_blocks_per_seq * block_size),
+ * or NULL to run one CTA per (sequence, kv head).  A block index outside the
+ * cache is skipped and sets QF_FLAG_BAD_BLOCK. */
+typedef struct {
+    const void* q; int64_t q_stride_seq, q_stride_head;
+    const void* k_cache; const void* v_cache; int64_t cache_strides[4];
+    int64_t num_blocks, block_size;
+    const int32_t* block_tables; int64_t block_tables_row_stride, max_blocks_per_seq;
+    const int32_t* seq_lens;
+    int64_t num_seqs, num_q_heads, num_kv_heads, head_dim;
+    float scale;
+    void* out; int64_t out_stride_seq, out_stride_head;
+    void* workspace; int64_t workspace_bytes;
+    int dtype;
+    int32_t* status;
+} qf_paged_attention_args;
+
+int qf_paged_attention_decode(const qf_paged_attention_args* args, cudaStream_t stream);
+
+/* Workspace bytes qf_paged_attention_decode needs to split sequences of up to
+ * max_seq_len tokens (0: nothing to split). */
+size_t qf_paged_attention_workspace_bytes(int64_t num_seqs, int64_t num_q_heads,
+                                          int64_t head_dim, int64_t max_seq_len);
+
+/* sizeof(qf_paged_attention_args) as compiled into the library. */
+size_t qf_paged_attention_args_size(void);
+
+/* ---------------------------------------------------------------------- */
 /* Status word: copy *status_dev to *flags_out (host) after the work queued
  * on `stream` so far, then zero it when `clear` is set.  Synchronises
  * `stream`.  Returns QF_ERR_DEVICE when any flag was set. */

@@ -16,6 +16,8 @@ reference path (citations are in the C source):
 * :func:`kv_store_batched` / :func:`kv_store_seq` -- ``server/model/kernels/
   kv_cache.py`` ``store_kv_cache_batched`` / ``store_kv_cache``
 * :func:`silu_and_mul`    -- ``Qwen3MLP`` activation product (HF:81-83)
+* :func:`paged_attention_decode` -- the reference's decode paged attention
+  (server/model/kernels/paged_attention.py:8-192), in torch fp32 on the CPU
 """
 
 from __future__ import annotations
@@ -233,4 +235,34 @@ def silu_and_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     out = torch.empty(T, I, dtype=gate.dtype)
     _check(lib().oracle_silu_and_mul(_p(gate), gate.stride(0), _p(up), up.stride(0), T, I,
                                      DTYPE_TAG[gate.dtype], _p(out), I), "silu_and_mul")
+    return out
+
+
+def paged_attention_decode(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                           block_tables: torch.Tensor, block_size: int,
+                           seq_lens: torch.Tensor) -> torch.Tensor:
+    """Decode paged attention as the reference defines it
+    (server/model/kernels/paged_attention.py:8-121, wrapper :124-192): for
+    sequence s and query head h, the first seq_lens[s] tokens of the sequence,
+    token j at cache[block_tables[s, j // block_size], h // (Hq // Hkv),
+    j % block_size], and out = softmax(q . K^T / sqrt(D)) @ V computed in
+    fp32, stored in the query's dtype."""
+    import math
+
+    query, k_cache, v_cache = _cpu(query), _cpu(k_cache), _cpu(v_cache)
+    block_tables, seq_lens = _cpu(block_tables), _cpu(seq_lens)
+    S, Hq, D = query.shape
+    Hkv = k_cache.shape[1]
+    G = Hq // Hkv
+    scale = 1.0 / math.sqrt(D)
+    out = torch.empty_like(query)
+    for s in range(S):
+        L = int(seq_lens[s])
+        nb = -(-L // block_size)
+        blocks = block_tables[s, :nb].long()
+        K = k_cache[blocks].permute(1, 0, 2, 3).reshape(Hkv, nb * block_size, D)[:, :L].float()
+        V = v_cache[blocks].permute(1, 0, 2, 3).reshape(Hkv, nb * block_size, D)[:, :L].float()
+        q = query[s].float().view(Hkv, G, D)
+        w = torch.softmax(torch.einsum("hgd,hkd->hgk", q, K) * scale, dim=-1)
+        out[s] = torch.einsum("hgk,hkd->hgd", w, V).reshape(Hq, D).to(query.dtype)
     return out

@@ -28,6 +28,9 @@ What produces the golden outputs:
 * ``outliers.pt`` -- Qwen3RMSNorm with the decoder layer's residual add at
   hidden 4096 with x50 outliers, and ACT2FN["silu"](gate) * up on
   large-magnitude inputs, in bf16.
+* ``paged_attention.pt`` -- the reference's decode paged-attention Triton
+  kernel (server/model/kernels/paged_attention.py) on its own tests'
+  configurations plus bf16 GQA cases longer than one partition.
 """
 
 from __future__ import annotations
@@ -312,14 +315,68 @@ def _outlier_case() -> dict:
             "h": h, "y": y, "gate": gate, "up": up, "act": act}
 
 
+def _paged_attention_case() -> dict:
+    """The reference's decode paged-attention Triton kernel
+    (server/model/kernels/paged_attention.py:124-192) under Triton's
+    interpreter on: the three configurations of its own tests
+    (tests/model/test_paged_attention_kernel.py:109-116) in fp32, its poisoned
+    partial-block case (:180-214), and bf16 GQA cases with sequences longer
+    than one 512-key partition (group sizes 4 and 8)."""
+    from server.model.kernels.paged_attention import paged_attention_forward
+
+    gen = torch.Generator().manual_seed(2024)
+    cases = []
+    for name, hq, hkv, hd, bsz, lens, dt, poison in (
+            ("mha-single-block", 4, 4, 64, 16, [10], torch.float32, False),
+            ("gqa-ragged", 8, 2, 64, 16, [7, 16, 40], torch.float32, False),
+            ("gqa-headdim128", 16, 4, 128, 32, [1, 33, 64], torch.float32, False),
+            ("partial-block-poisoned", 8, 2, 64, 16, [5], torch.float32, True),
+            ("bf16-g4-split", 8, 2, 128, 16, [1, 15, 17, 300, 700], torch.bfloat16, False),
+            ("bf16-g8-split", 16, 2, 128, 16, [33, 600], torch.bfloat16, False)):
+        per = [max(1, -(-n // bsz)) for n in lens]
+        nblk = sum(per) + 3
+        q = torch.randn(len(lens), hq, hd, generator=gen).to(dt)
+        kc = torch.randn(nblk, hkv, bsz, hd, generator=gen).to(dt)
+        vc = torch.randn(nblk, hkv, bsz, hd, generator=gen).to(dt)
+        phys = torch.randperm(nblk, generator=gen)[:sum(per)]
+        bt = torch.zeros(len(lens), max(per), dtype=torch.int32)
+        cur = 0
+        for i, n in enumerate(per):
+            bt[i, :n] = phys[cur:cur + n].to(torch.int32)
+            cur += n
+        if poison:
+            blk = int(bt[0, 0])
+            kc[blk, :, lens[0]:, :] = 1e4
+            vc[blk, :, lens[0]:, :] = 1e4
+        sl = torch.tensor(lens, dtype=torch.int32)
+        out = paged_attention_forward(q, kc, vc, bt, bsz, sl)
+        case = {"name": name, "query": q, "k_cache": kc, "v_cache": vc, "block_tables": bt,
+                "block_size": bsz, "seq_lens": sl, "out": out}
+        if dt != torch.float32:
+            # The kernel upcasts its loads to fp32 (paged_attention.py:72, :90-95), so the
+            # same kernel on fp32 copies of the inputs gives its exact fp32 result before
+            # the final store.  Triton's interpreter stores fp32 into a bf16 tensor by
+            # truncation, while the GPU rounds to nearest even; the expected bf16 output
+            # is out_f32 rounded to nearest even.
+            case["out_f32"] = paged_attention_forward(q.float(), kc.float(), vc.float(), bt,
+                                                      bsz, sl)
+        cases.append(case)
+    return {"cases": cases}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("TINYSERVER_REF", "/root/reference"))
+    ap.add_argument("--only", default=None, help="write just this fixture (e.g. paged_attention)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     import transformers
     torch.manual_seed(0)
     meta = {"transformers": transformers.__version__, "torch": torch.__version__}
+    if args.only == "paged_attention":
+        torch.save({**_paged_attention_case(), "meta": meta},
+                   os.path.join(HERE, "paged_attention.pt"))
+        return
     for dt, lens, seed, vocab, nblk, fname in (
             (torch.bfloat16, [5, 16, 37], 1234, 128, 8, "layer_bf16.pt"),
             (torch.float32, [3, 17], 1235, 128, 4, "layer_f32.pt")):
@@ -329,6 +386,7 @@ def main() -> None:
     torch.save({**_kv_store_case(), "meta": meta}, os.path.join(HERE, "kv_store.pt"))
     torch.save({**_rope_case(), "meta": meta}, os.path.join(HERE, "rope_cos_sin.pt"))
     torch.save({**_outlier_case(), "meta": meta}, os.path.join(HERE, "outliers.pt"))
+    torch.save({**_paged_attention_case(), "meta": meta}, os.path.join(HERE, "paged_attention.pt"))
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".pt"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

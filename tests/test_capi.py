@@ -29,7 +29,8 @@ def test_header_declares_the_expected_entry_points():
     names = declared_functions()
     for required in ("qf_kv_store_batched", "qf_kv_store_seq", "qf_rmsnorm", "qf_add_rmsnorm",
                      "qf_rope_cos_sin", "qf_qk_norm_rope_store", "qf_silu_and_mul",
-                     "qf_embedding", "qf_build_slot_mapping", "qf_read_status"):
+                     "qf_embedding", "qf_build_slot_mapping", "qf_paged_attention_decode",
+                     "qf_paged_attention_workspace_bytes", "qf_read_status"):
         assert required in names
 
 

@@ -88,3 +88,25 @@ def test_unsupported_dtypes_raise():
     with pytest.raises(ValueError, match="dtype"):
         tsb.rms_norm(torch.zeros(2, 8, dtype=torch.float64), torch.ones(8, dtype=torch.float64),
                      1e-6)
+
+
+def test_paged_attention_rejects_a_2d_query():
+    """Same guard as the reference (paged_attention.py:171-172), before any device work."""
+    from tinyserver_b200 import paged_attention_forward
+
+    query = torch.zeros(4, 64)
+    k_cache = torch.zeros(2, 4, 16, 64)
+    with pytest.raises(ValueError, match="3D"):
+        paged_attention_forward(query, k_cache, torch.zeros_like(k_cache),
+                                torch.zeros(1, 1, dtype=torch.int32), 16,
+                                torch.ones(1, dtype=torch.int32))
+
+
+def test_paged_attention_rejects_cpu_tensors():
+    from tinyserver_b200 import paged_attention_forward
+
+    k_cache = torch.zeros(2, 4, 16, 64)
+    with pytest.raises(ValueError, match="CUDA tensors only"):
+        paged_attention_forward(torch.zeros(1, 4, 64), k_cache, torch.zeros_like(k_cache),
+                                torch.zeros(1, 1, dtype=torch.int32), 16,
+                                torch.ones(1, dtype=torch.int32))

@@ -196,3 +196,22 @@ def test_kv_store_rejects_out_of_range_slot():
     with pytest.raises(IndexError):
         oracle.kv_store_batched(k, k, kc, vc, torch.tensor([0, 1, 1]), torch.tensor([0, 1, 4]))
     assert not kc.any() and not vc.any()
+
+
+def test_paged_attention_decode_matches_reference_kernel():
+    """The oracle against the reference's own Triton decode attention (run
+    under Triton's interpreter when the fixture was made)."""
+    g = load_golden("paged_attention.pt")
+    for c in g["cases"]:
+        out = oracle.paged_attention_decode(c["query"], c["k_cache"], c["v_cache"],
+                                            c["block_tables"], c["block_size"], c["seq_lens"])
+        if c["out"].dtype == torch.float32:
+            torch.testing.assert_close(out, c["out"], atol=1e-5, rtol=1e-5, msg=c["name"])
+        else:
+            # the reference's fp32 result, rounded to nearest even as the GPU stores it
+            assert_close(out, c["out_f32"].to(c["out"].dtype), c["name"], min_exact=0.99)
+            out32 = oracle.paged_attention_decode(
+                c["query"].float(), c["k_cache"].float(), c["v_cache"].float(),
+                c["block_tables"], c["block_size"], c["seq_lens"])
+            torch.testing.assert_close(out32, c["out_f32"], atol=1e-5, rtol=1e-5, msg=c["name"])
+        assert torch.isfinite(out).all(), c["name"]

@@ -53,6 +53,26 @@ class QkNormRopeArgs(ctypes.Structure):
     ]
 
 
+class PagedAttentionArgs(ctypes.Structure):
+    """Mirror of qf_paged_attention_args (field order and types must match)."""
+
+    _fields_ = [
+        ("q", c_vp), ("q_stride_seq", c_i64), ("q_stride_head", c_i64),
+        ("k_cache", c_vp), ("v_cache", c_vp), ("cache_strides", c_i64 * 4),
+        ("num_blocks", c_i64), ("block_size", c_i64),
+        ("block_tables", c_vp), ("block_tables_row_stride", c_i64),
+        ("max_blocks_per_seq", c_i64),
+        ("seq_lens", c_vp),
+        ("num_seqs", c_i64), ("num_q_heads", c_i64), ("num_kv_heads", c_i64),
+        ("head_dim", c_i64),
+        ("scale", c_float),
+        ("out", c_vp), ("out_stride_seq", c_i64), ("out_stride_head", c_i64),
+        ("workspace", c_vp), ("workspace_bytes", c_i64),
+        ("dtype", c_int),
+        ("status", c_vp),
+    ]
+
+
 # name -> argtypes of every exported entry point (restype int unless listed below)
 SIGNATURES: dict[str, list] = {
     "qf_kv_store_batched": [c_vp, I64P, c_vp, I64P, c_vp, I64P, c_vp, I64P, c_vp, c_vp, c_int,
@@ -70,12 +90,17 @@ SIGNATURES: dict[str, list] = {
                      c_vp],
     "qf_build_slot_mapping": [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp,
                               c_vp, c_vp],
+    "qf_paged_attention_decode": [ctypes.POINTER(PagedAttentionArgs), c_vp],
+    "qf_paged_attention_workspace_bytes": [c_i64, c_i64, c_i64, c_i64],
+    "qf_paged_attention_args_size": [],
     "qf_read_status": [c_vp, ctypes.POINTER(ctypes.c_int32), c_int, c_vp],
     "qf_last_cuda_error": [],
     "qf_version": [],
 }
 RESTYPES = {"qf_last_cuda_error": ctypes.c_char_p, "qf_version": ctypes.c_char_p,
-            "qf_qk_norm_rope_args_size": ctypes.c_size_t}
+            "qf_qk_norm_rope_args_size": ctypes.c_size_t,
+            "qf_paged_attention_args_size": ctypes.c_size_t,
+            "qf_paged_attention_workspace_bytes": ctypes.c_size_t}
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
@@ -124,10 +149,12 @@ def lib() -> ctypes.CDLL:
                 fn = getattr(handle, name)
                 fn.argtypes = argtypes
                 fn.restype = RESTYPES.get(name, c_int)
-            size = handle.qf_qk_norm_rope_args_size()
-            if size != ctypes.sizeof(QkNormRopeArgs):
-                raise RuntimeError(f"qf_qk_norm_rope_args ABI mismatch: library {size} bytes, "
-                                   f"binding {ctypes.sizeof(QkNormRopeArgs)} bytes")
+            for fn, mirror in (("qf_qk_norm_rope_args_size", QkNormRopeArgs),
+                               ("qf_paged_attention_args_size", PagedAttentionArgs)):
+                size = getattr(handle, fn)()
+                if size != ctypes.sizeof(mirror):
+                    raise RuntimeError(f"{fn}: ABI mismatch, library {size} bytes, binding "
+                                       f"{ctypes.sizeof(mirror)} bytes")
             _lib = handle
     return _lib
 

@@ -1,0 +1,378 @@
+// Decode-phase paged attention over the (N, Hkv, B, D) KV pages.
+//
+// Replaces paged_attention_forward (server/model/kernels/paged_attention.py:
+// 124-192; Triton kernel :8-121): for every sequence s and query head h, one
+// query token against the sequence's first seq_lens[s] cached tokens,
+//   out[s, h, :] = softmax(q[s, h] . K_s^T * scale) @ V_s       (fp32 math)
+// with K_s/V_s gathered through block_tables[s] (token j at block
+// block_tables[s, j / B], slot j % B) and kv head h / (Hq / Hkv) (GQA).
+//
+// B200 shape of the computation (flash-decoding):
+//  * one CTA per (sequence, kv head, partition of kPart keys); the CTA serves
+//    all G = Hq/Hkv query heads of its kv head, so every K and V row crosses
+//    HBM once per layer, not once per query head (the reference's grid is
+//    (sequence, query head));
+//  * 4 warps take 32-key tiles in turn; in QK a lane owns one key and walks
+//    its row with 16-byte loads against q in shared memory (broadcast reads);
+//    online softmax per warp and head in fp32; in PV a lane owns D/32
+//    elements of the output and reads each V row coalesced;
+//  * the warps merge through shared memory; a sequence longer than one
+//    partition leaves per-partition (max, sum, acc) in a caller-provided fp32
+//    workspace and a second kernel merges them.
+// Keys past seq_len are never read; a block index outside the cache is
+// skipped and flagged (QF_FLAG_BAD_BLOCK).
+#include <math.h>
+
+#include "qf_common.cuh"
+
+// Keys per CTA when a workspace allows splitting a sequence (compile-time knob).
+#ifndef QF_ATTN_PARTITION
+#define QF_ATTN_PARTITION 512
+#endif
+
+namespace qf {
+namespace {
+
+constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = 32 * kAttnWarps;
+
+struct AttnDev {
+    const char* q;
+    int64_t qs, qh;  // query strides (sequence, head), elements
+    const char* kc;
+    const char* vc;
+    int64_t c0, c1, c2;  // cache strides (block, head, slot), elements
+    int64_t N, B;
+    const int32_t* bt;
+    int64_t bts, max_blocks;
+    const int32_t* lens;
+    int S, Hq, Hkv;
+    float scale;
+    char* out;
+    int64_t os, oh;
+    float* ws;  // [S][Hq][P][D + 2]: acc[0:D], max, sum
+    int P;      // partitions per sequence in the workspace layout
+    int part;   // keys per partition
+    int32_t* status;
+};
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// exp(x - m) that is 0 when m is -inf (no key seen yet) instead of NaN.
+__device__ __forceinline__ float exp_rel(float x, float m) {
+    return m == -INFINITY ? 0.f : __expf(x - m);
+}
+
+// Load PER elements of one row (PER * sizeof(T) bytes: 4, 8 or a multiple of
+// 16) as floats.
+template <typename T, int PER>
+__device__ __forceinline__ void load_row_slice(const char* p, float* f) {
+    constexpr int BYTES = PER * (int)sizeof(T);
+    if constexpr (BYTES % 16 == 0) {
+#pragma unroll
+        for (int c = 0; c < BYTES / 16; ++c) unpack<T>(ld_shared_ro16(p + c * 16), f + c * Dt<T>::kPerVec);
+    } else {
+        static_assert(BYTES == 4 || BYTES == 8, "slice size");
+        uint2 r;
+        if constexpr (BYTES == 8) r = __ldg(reinterpret_cast<const uint2*>(p));
+        else r = make_uint2(__ldg(reinterpret_cast<const unsigned*>(p)), 0);
+        const T* e = reinterpret_cast<const T*>(&r);
+#pragma unroll
+        for (int i = 0; i < PER; ++i) f[i] = Dt<T>::to_f(e[i]);
+    }
+}
+
+template <typename T, int D, int G>
+__global__ void __launch_bounds__(kAttnThreads) paged_decode_kernel(const AttnDev a) {
+    constexpr int ES = sizeof(T);
+    constexpr int EPV = 16 / ES;       // elements per 16-byte chunk
+    constexpr int NCH = D / EPV;       // 16-byte chunks per row
+    constexpr int PER = D / 32;        // output elements per lane in PV
+    const int p = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
+    const int L = __ldg(a.lens + s);
+    const int k_begin = p * a.part;
+    if (p > 0 && k_begin >= L) return;  // partition past the sequence (p = 0 always runs)
+    const int k_end = min(L, k_begin + a.part);
+    const int nparts = L > a.part ? (L + a.part - 1) / a.part : 1;
+
+    __shared__ __align__(16) float qs[G][D];
+    __shared__ float ps[kAttnWarps][G][32];
+    __shared__ float wm[kAttnWarps][G], wl[kAttnWarps][G];
+    __shared__ __align__(16) float wacc[kAttnWarps][G][D];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < G * D; i += kAttnThreads) {
+        const int h = i / D, d = i - h * D;
+        const T* qp = reinterpret_cast<const T*>(a.q) + (int64_t)s * a.qs +
+                      (int64_t)(g * G + h) * a.qh + d;
+        qs[h][d] = Dt<T>::to_f(*qp);
+    }
+    __syncthreads();
+
+    float m[G], l[G], acc[G][PER];
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        m[h] = -INFINITY;
+        l[h] = 0.f;
+#pragma unroll
+        for (int e = 0; e < PER; ++e) acc[h][e] = 0.f;
+    }
+
+    const int ntiles = (k_end - k_begin + 31) / 32;
+    const int32_t* bt = a.bt + (int64_t)s * a.bts;
+    for (int tile = warp; tile < ntiles; tile += kAttnWarps) {
+        const int j0 = k_begin + tile * 32;
+        const int j = j0 + lane;
+        bool valid = j < k_end;
+        int64_t row_off = 0;  // (block, head g, slot) element offset of key j
+        if (valid) {
+            const int64_t lb = j / a.B;
+            const int64_t blk = __ldg(bt + lb);
+            if (blk < 0 || blk >= a.N) {
+                flag(a.status, QF_FLAG_BAD_BLOCK);
+                valid = false;
+            } else {
+                row_off = blk * a.c0 + (int64_t)g * a.c1 + (j - lb * a.B) * a.c2;
+            }
+        }
+
+        // QK: lane = key, the row in 16-byte chunks, 8 in flight
+        float sc[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) sc[h] = 0.f;
+        if (valid) {
+            const char* kr = a.kc + row_off * ES;
+#pragma unroll
+            for (int c0 = 0; c0 < NCH; c0 += 8) {
+                uint4 kv[8];
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    if (c0 + c < NCH) kv[c] = ld_stream16(kr + (c0 + c) * 16);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    if (c0 + c >= NCH) break;
+                    float x[EPV];
+                    unpack<T>(kv[c], x);
+#pragma unroll
+                    for (int h = 0; h < G; ++h) {
+                        const float* qv = &qs[h][(c0 + c) * EPV];
+#pragma unroll
+                        for (int e = 0; e < EPV; ++e) sc[h] = fmaf(qv[e], x[e], sc[h]);
+                    }
+                }
+            }
+        }
+
+        // online softmax, per head
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+            const float v = valid ? sc[h] * a.scale : -INFINITY;
+            const float mnew = fmaxf(m[h], warp_max(v));
+            const float pj = valid ? exp_rel(v, mnew) : 0.f;
+            const float corr = exp_rel(m[h], mnew);
+            l[h] = l[h] * corr + warp_sum(pj);
+#pragma unroll
+            for (int e = 0; e < PER; ++e) acc[h][e] *= corr;
+            m[h] = mnew;
+            ps[warp][h][lane] = pj;
+        }
+        __syncwarp();
+
+        // PV: lane = D/32 output elements; each valid key's V row, coalesced
+        const int nk = min(32, k_end - j0);
+        for (int jj = 0; jj < nk; ++jj) {
+            const int64_t off = __shfl_sync(0xffffffffu, row_off, jj);
+            const bool ok = __shfl_sync(0xffffffffu, (int)valid, jj) != 0;
+            if (!ok) continue;
+            float v[PER];
+            load_row_slice<T, PER>(a.vc + (off + lane * PER) * ES, v);
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                const float pj = ps[warp][h][jj];
+#pragma unroll
+                for (int e = 0; e < PER; ++e) acc[h][e] = fmaf(pj, v[e], acc[h][e]);
+            }
+        }
+        __syncwarp();
+    }
+
+    // merge the warps
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        if (lane == 0) {
+            wm[warp][h] = m[h];
+            wl[warp][h] = l[h];
+        }
+#pragma unroll
+        for (int e = 0; e < PER; ++e) wacc[warp][h][lane * PER + e] = acc[h][e];
+    }
+    __syncthreads();
+    for (int i = tid; i < G * D; i += kAttnThreads) {
+        const int h = i / D, d = i - h * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w][h]);
+        float Ls = 0.f, A = 0.f;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) {
+            const float f = exp_rel(wm[w][h], M);
+            Ls += wl[w][h] * f;
+            A += wacc[w][h][d] * f;
+        }
+        const int hq = g * G + h;
+        if (nparts == 1) {
+            T* o = reinterpret_cast<T*>(a.out) + (int64_t)s * a.os + (int64_t)hq * a.oh;
+            o[d] = Dt<T>::from_f(A / Ls);
+        } else {
+            float* w = a.ws + (((int64_t)s * a.Hq + hq) * a.P + p) * (D + 2);
+            w[d] = A;
+            if (d == 0) {
+                w[D] = M;
+                w[D + 1] = Ls;
+            }
+        }
+    }
+}
+
+// Merge the partitions of sequences longer than one partition.
+template <typename T, int D>
+__global__ void __launch_bounds__(128) paged_decode_merge_kernel(const AttnDev a) {
+    const int hq = blockIdx.x, s = blockIdx.y;
+    const int L = __ldg(a.lens + s);
+    const int nparts = L > a.part ? (L + a.part - 1) / a.part : 1;
+    if (nparts == 1) return;
+    const float* w = a.ws + ((int64_t)s * a.Hq + hq) * a.P * (D + 2);
+    float M = -INFINITY;
+    for (int p = 0; p < nparts; ++p) M = fmaxf(M, w[p * (D + 2) + D]);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float Ls = 0.f, A = 0.f;
+        for (int p = 0; p < nparts; ++p) {
+            const float* wp = w + p * (D + 2);
+            const float f = exp_rel(wp[D], M);
+            Ls += wp[D + 1] * f;
+            A += wp[d] * f;
+        }
+        T* o = reinterpret_cast<T*>(a.out) + (int64_t)s * a.os + (int64_t)hq * a.oh;
+        o[d] = Dt<T>::from_f(A / Ls);
+    }
+}
+
+template <typename T, int D, int G>
+int launch_attn(const AttnDev& a, cudaStream_t stream) {
+    const dim3 grid((unsigned)a.P, (unsigned)a.Hkv, (unsigned)a.S);
+    paged_decode_kernel<T, D, G><<<grid, kAttnThreads, 0, stream>>>(a);
+    int rc = check_launch();
+    if (rc || a.P == 1) return rc;
+    paged_decode_merge_kernel<T, D><<<dim3((unsigned)a.Hq, (unsigned)a.S), 128, 0, stream>>>(a);
+    return check_launch();
+}
+
+template <typename T, int D>
+int dispatch_g(const AttnDev& a, int G, cudaStream_t stream) {
+    switch (G) {
+    case 1: return launch_attn<T, D, 1>(a, stream);
+    case 2: return launch_attn<T, D, 2>(a, stream);
+    case 4: return launch_attn<T, D, 4>(a, stream);
+    case 8: return launch_attn<T, D, 8>(a, stream);
+    default: return QF_ERR_UNSUPPORTED;
+    }
+}
+
+template <typename T>
+int dispatch_d(const AttnDev& a, int64_t D, int G, cudaStream_t stream) {
+    switch (D) {
+    case 64: return dispatch_g<T, 64>(a, G, stream);
+    case 128: return dispatch_g<T, 128>(a, G, stream);
+    case 256: return dispatch_g<T, 256>(a, G, stream);
+    default: return QF_ERR_UNSUPPORTED;
+    }
+}
+
+int partitions(int64_t max_seq_len, int64_t part) {
+    return (int)std::max<int64_t>(1, ceil_div(max_seq_len, part));
+}
+
+}  // namespace
+}  // namespace qf
+
+extern "C" size_t qf_paged_attention_workspace_bytes(int64_t num_seqs, int64_t num_q_heads,
+                                                     int64_t head_dim, int64_t max_seq_len) {
+    if (num_seqs <= 0 || num_q_heads <= 0 || head_dim <= 0 || max_seq_len <= 0) return 0;
+    const int64_t P = qf::partitions(max_seq_len, QF_ATTN_PARTITION);
+    if (P == 1) return 0;
+    return (size_t)(num_seqs * num_q_heads * P * (head_dim + 2) * (int64_t)sizeof(float));
+}
+
+extern "C" int qf_paged_attention_decode(const qf_paged_attention_args* p, cudaStream_t stream) {
+    if (!p) return QF_ERR_INVALID;
+    const qf_paged_attention_args& g = *p;
+    if (g.num_seqs < 0 || g.num_q_heads <= 0 || g.num_kv_heads <= 0 || g.block_size <= 0 ||
+        g.num_blocks < 0 || g.max_blocks_per_seq < 0)
+        return QF_ERR_INVALID;
+    if (g.num_seqs == 0) return QF_OK;
+    if (!g.q || !g.k_cache || !g.v_cache || !g.block_tables || !g.seq_lens || !g.out)
+        return QF_ERR_INVALID;
+    if (g.num_q_heads % g.num_kv_heads) return QF_ERR_INVALID;
+    if (g.num_seqs > 65535 || g.num_kv_heads > 65535) return QF_ERR_UNSUPPORTED;
+    const int64_t D = g.head_dim;
+    const int64_t es = g.dtype == QF_F32 ? 4 : 2;
+    if (g.dtype != QF_F32 && g.dtype != QF_F16 && g.dtype != QF_BF16) return QF_ERR_INVALID;
+    // K rows are read in 16-byte chunks, V row slices in D/32-element pieces
+    if ((D * es) % 16 || (g.cache_strides[0] * es) % 16 || (g.cache_strides[1] * es) % 16 ||
+        (g.cache_strides[2] * es) % 16 || g.cache_strides[3] != 1 || !qf::aligned16(g.k_cache) ||
+        !qf::aligned16(g.v_cache))
+        return QF_ERR_UNSUPPORTED;
+    qf::AttnDev a{};
+    a.q = static_cast<const char*>(g.q);
+    a.qs = g.q_stride_seq;
+    a.qh = g.q_stride_head;
+    a.kc = static_cast<const char*>(g.k_cache);
+    a.vc = static_cast<const char*>(g.v_cache);
+    a.c0 = g.cache_strides[0];
+    a.c1 = g.cache_strides[1];
+    a.c2 = g.cache_strides[2];
+    a.N = g.num_blocks;
+    a.B = g.block_size;
+    a.bt = g.block_tables;
+    a.bts = g.block_tables_row_stride;
+    a.max_blocks = g.max_blocks_per_seq;
+    a.lens = g.seq_lens;
+    a.S = (int)g.num_seqs;
+    a.Hq = (int)g.num_q_heads;
+    a.Hkv = (int)g.num_kv_heads;
+    a.scale = g.scale;
+    a.out = static_cast<char*>(g.out);
+    a.os = g.out_stride_seq;
+    a.oh = g.out_stride_head;
+    a.status = g.status;
+    // the longest sequence the block tables can describe bounds the partitions
+    const int64_t max_len = std::max<int64_t>(1, g.max_blocks_per_seq * g.block_size);
+    const int64_t need = (int64_t)qf_paged_attention_workspace_bytes(g.num_seqs, g.num_q_heads,
+                                                                     D, max_len);
+    if (need > 0 && g.workspace && g.workspace_bytes >= need) {
+        a.part = QF_ATTN_PARTITION;
+        a.P = qf::partitions(max_len, a.part);
+        a.ws = static_cast<float*>(g.workspace);
+    } else if (need > 0 && g.workspace) {
+        return QF_ERR_INVALID;  // a workspace was given but is too small
+    } else {
+        a.part = (int)std::min<int64_t>(max_len, 1 << 30);  // one partition per sequence
+        a.P = 1;
+        a.ws = nullptr;
+    }
+    const int G = (int)(g.num_q_heads / g.num_kv_heads);
+    switch (g.dtype) {
+    case QF_F32: return qf::dispatch_d<float>(a, D, G, stream);
+    case QF_F16: return qf::dispatch_d<__half>(a, D, G, stream);
+    default: return qf::dispatch_d<__nv_bfloat16>(a, D, G, stream);
+    }
+}
