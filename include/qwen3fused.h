@@ -38,7 +38,9 @@ enum {
     QF_ERR_INVALID = 1,     /* null pointer, negative size, unknown tag */
     QF_ERR_UNSUPPORTED = 2, /* a shape this library has no kernel for */
     QF_ERR_LAUNCH = 3,      /* the CUDA launch failed (see qf_last_cuda_error) */
-    QF_ERR_DEVICE = 4       /* qf_read_status found a flagged index error */
+    QF_ERR_DEVICE = 4,      /* qf_read_status found a flagged index error */
+    QF_ERR_SCRATCH = 5      /* the call needs more scratch than the fixed array of
+                               qf_paged_attention_decode_noalloc holds */
 };
 
 enum {
@@ -238,6 +240,30 @@ size_t qf_paged_attention_workspace_bytes(int64_t num_seqs, int64_t num_q_heads,
 
 /* sizeof(qf_paged_attention_args) as compiled into the library. */
 size_t qf_paged_attention_args_size(void);
+
+/* The same decode attention for callers that cannot allocate device memory.
+ * No counterpart in the reference.  Some callers must not call cudaMalloc: a
+ * host framework that hands this library only raw pointers and owns every
+ * allocation, a runtime that reserves all device memory at start, or a
+ * latency-bound loop that cannot take the device synchronisation an
+ * allocation implies.  This entry point allocates nothing: the split-K
+ * partials live in a fixed device array of qf_paged_attention_noalloc_capacity()
+ * bytes (128 MiB) inside the library, which every GPU that loads the library
+ * holds until the process exits.  args->workspace and workspace_bytes are
+ * ignored; q, caches, tables and out are still the caller's.
+ *  - A call whose partials would exceed the array (see
+ *    qf_paged_attention_workspace_bytes) returns QF_ERR_SCRATCH before any
+ *    device work.
+ *  - The first call on each device looks up the array's device address with
+ *    cudaGetSymbolAddress (with that device current); make that first call
+ *    before any stream capture.
+ *  - All calls on a device share the array and it keeps the last call's
+ *    contents (nothing in it needs to start at zero); calls that overlap on
+ *    the GPU, e.g. on two streams, race on it. */
+int qf_paged_attention_decode_noalloc(const qf_paged_attention_args* args, cudaStream_t stream);
+
+/* Bytes of the fixed array qf_paged_attention_decode_noalloc uses. */
+size_t qf_paged_attention_noalloc_capacity(void);
 
 /* ---------------------------------------------------------------------- */
 /* Status word: copy *status_dev to *flags_out (host) after the work queued

@@ -23,6 +23,7 @@ I64P = ctypes.POINTER(ctypes.c_int64)
 QF_F32, QF_F16, QF_BF16 = 0, 1, 2
 QF_I32, QF_I64 = 0, 1
 QF_OK, QF_ERR_INVALID, QF_ERR_UNSUPPORTED, QF_ERR_LAUNCH, QF_ERR_DEVICE = 0, 1, 2, 3, 4
+QF_ERR_SCRATCH = 5
 QF_FLAG_BAD_BLOCK, QF_FLAG_BAD_SLOT, QF_FLAG_BAD_TOKEN, QF_FLAG_BAD_TABLE = 1, 2, 4, 8
 
 FLAG_NAMES = {QF_FLAG_BAD_BLOCK: "block index outside the cache",
@@ -93,6 +94,8 @@ SIGNATURES: dict[str, list] = {
     "qf_paged_attention_decode": [ctypes.POINTER(PagedAttentionArgs), c_vp],
     "qf_paged_attention_workspace_bytes": [c_i64, c_i64, c_i64, c_i64],
     "qf_paged_attention_args_size": [],
+    "qf_paged_attention_decode_noalloc": [ctypes.POINTER(PagedAttentionArgs), c_vp],
+    "qf_paged_attention_noalloc_capacity": [],
     "qf_read_status": [c_vp, ctypes.POINTER(ctypes.c_int32), c_int, c_vp],
     "qf_last_cuda_error": [],
     "qf_version": [],
@@ -100,7 +103,8 @@ SIGNATURES: dict[str, list] = {
 RESTYPES = {"qf_last_cuda_error": ctypes.c_char_p, "qf_version": ctypes.c_char_p,
             "qf_qk_norm_rope_args_size": ctypes.c_size_t,
             "qf_paged_attention_args_size": ctypes.c_size_t,
-            "qf_paged_attention_workspace_bytes": ctypes.c_size_t}
+            "qf_paged_attention_workspace_bytes": ctypes.c_size_t,
+            "qf_paged_attention_noalloc_capacity": ctypes.c_size_t}
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

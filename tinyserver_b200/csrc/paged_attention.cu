@@ -376,3 +376,68 @@ extern "C" int qf_paged_attention_decode(const qf_paged_attention_args* p, cudaS
     default: return qf::dispatch_d<__nv_bfloat16>(a, D, G, stream);
     }
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.  Some callers cannot allocate device memory: a
+// host framework that hands this library only raw pointers and owns every
+// allocation itself, a runtime that reserves all device memory once at start
+// and forbids cudaMalloc afterwards, or a latency-bound loop where the device
+// synchronisation that cudaMalloc/cudaFree imply is not acceptable.  They
+// call qf_paged_attention_decode_noalloc, whose split-K partials live in the
+// fixed array below instead of a caller workspace.
+//
+// The array is a file-scope device global: every GPU that loads this library
+// holds its kNoAllocScratchBytes until the process exits.  All calls on a
+// device share it and it keeps the last call's contents; nothing in it has to
+// start at zero (each call writes every partial it later reads), but calls
+// that overlap on the GPU (two streams, two threads) race on it.
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(128) << 20;  // 128 MiB
+__device__ __align__(256) unsigned char g_attn_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kMaxDevices];  // device address of g_attn_scratch, per device
+
+// The array's device address on the current device.  In host code the
+// array's name is only a host-side stand-in, so the address is looked up with
+// cudaGetSymbolAddress, once per device, with that device current.
+int scratch_address(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return qf::launch_failed(e);
+    if (dev < 0 || dev >= kMaxDevices) return QF_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_ptr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_attn_scratch);
+        if (e != cudaSuccess) return qf::launch_failed(e);
+        g_scratch_ptr[dev] = p;
+    }
+    *out = g_scratch_ptr[dev];
+    return QF_OK;
+}
+}  // namespace
+
+extern "C" size_t qf_paged_attention_noalloc_capacity(void) { return kNoAllocScratchBytes; }
+
+extern "C" int qf_paged_attention_decode_noalloc(const qf_paged_attention_args* p,
+                                                 cudaStream_t stream) {
+    if (!p) return QF_ERR_INVALID;
+    const int64_t max_len = std::max<int64_t>(1, p->max_blocks_per_seq * p->block_size);
+    if (p->num_seqs > 0 && p->num_q_heads > 0 && p->head_dim > 0 &&
+        qf_paged_attention_workspace_bytes(p->num_seqs, p->num_q_heads, p->head_dim, max_len) >
+            kNoAllocScratchBytes)
+        return QF_ERR_SCRATCH;  // checked before any device work
+    qf_paged_attention_args a = *p;
+    a.workspace = nullptr;
+    a.workspace_bytes = 0;
+    if (a.num_seqs > 0) {
+        void* ptr = nullptr;
+        const int rc = scratch_address(&ptr);
+        if (rc) return rc;
+        a.workspace = ptr;
+        a.workspace_bytes = (int64_t)kNoAllocScratchBytes;
+    }
+    return qf_paged_attention_decode(&a, stream);
+}
