@@ -509,6 +509,80 @@ def run_reference(args, rank: int) -> dict | None:
 
 
 # ----------------------------------------------------------------------------
+def run_attention(args, rank: int, world: int, local_rank: int) -> dict | None:
+    """--workload attn: decode paged attention (the next row after the fused
+    path) on config c3: 256 sequences, one new token each at positions
+    U[1, 8191] (context = position + 1), Qwen3-8B heads (32 q / 8 kv,
+    head_dim 128), 16-token pages in a 32768-block cache, bf16.  Algorithmic
+    bytes: every context token's K and V row of every kv head once, plus q
+    and out."""
+    import tinyserver_b200 as tsb
+    from tinyserver_b200 import workloads as W
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = W.CONFIGS["c3"]
+    s = cfg.shape
+    b = W.index_data(cfg, shard=rank)
+    lens = (b.positions + 1).to(torch.int32)  # each sequence's one token attends to 0..pos
+    S, Hq, Hkv, D, B = len(b.seqs), s.num_q_heads, s.num_kv_heads, s.head_dim, cfg.block_size
+    g = torch.Generator(device=dev).manual_seed(W.seed_of(cfg, rank) + 5)
+    pool = torch.randn(2, cfg.num_blocks, Hkv, B, D, generator=g, device=dev,
+                       dtype=torch.float32).to(cfg.dtype)
+    q = torch.randn(S, Hq, D, generator=g, device=dev, dtype=torch.float32).to(cfg.dtype)
+    bt = b.block_tables.to(dev)
+    sl = lens.to(dev)
+    ws = torch.empty(tsb.paged_attention_workspace_bytes(S, Hq, D, bt.shape[1] * B) // 4 + 1,
+                     dtype=torch.float32, device=dev)
+
+    def once():
+        return tsb.paged_attention_forward(q, pool[0], pool[1], bt, B, sl, workspace=ws)
+
+    for _ in range(max(args.warmup, 3)):
+        once()
+    tsb.check_errors(dev)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local_rank).start()
+    e0.record()
+    for _ in range(args.steps):
+        once()
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    tsb.check_errors(dev)
+    if world > 1:
+        m = torch.tensor([ms], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(m, op=torch.distributed.ReduceOp.MAX)
+        ms = float(m.item())
+    if rank != 0:
+        return None
+    peak, peak_kind = hbm_peak()
+    ctx = int(lens.sum())
+    nbytes = ctx * Hkv * D * 2 * 2 + 2 * S * Hq * D * 2 + S * (bt.shape[1] + 1) * 4
+    per_ms = ms / args.steps
+    gbs = nbytes / (per_ms * 1e-3) / 1e9
+    return {
+        "metric": "decode paged attention tokens/s and HBM GB/s per B200, Qwen3-8B heads",
+        "value": round(world * S / (per_ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded positions and cache contents of config c3",
+        "config": {"workload": "c3 decode attention: 256 sequences x 1 token, context "
+                               f"{ctx} tokens in all, 16-token pages, 32768 blocks",
+                   "context_tokens": ctx, "l2": f"{nbytes / 1e9:.2f} GB read per step (> L2)"},
+        "roofline": {"bound": "hbm", "kernel": "paged_decode_mma_kernel + merge",
+                     "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs / peak, 4), "algorithmic_bytes_per_launch": nbytes,
+                     "traffic": None},
+        "gpu_launches": 2 * args.steps, "clocks": clocks,
+    }
+
+
+# ----------------------------------------------------------------------------
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -525,6 +599,8 @@ def main() -> None:
                     help="CPU-baseline timing budget (ours arm)")
     ap.add_argument("--cpu-total", type=float, default=90.0,
                     help="total CPU time budget of the --impl reference run")
+    ap.add_argument("--workload", choices=["layer", "attn"], default="layer",
+                    help="layer: the fused-layer step (the headline); attn: decode attention")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -542,7 +618,10 @@ def main() -> None:
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
     try:
-        line = run_ours(args, rank, world, local_rank)
+        if args.workload == "attn":
+            line = run_attention(args, rank, world, local_rank)
+        else:
+            line = run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()

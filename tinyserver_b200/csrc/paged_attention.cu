@@ -35,6 +35,10 @@ namespace {
 
 constexpr int kAttnWarps = 4;
 constexpr int kAttnThreads = 32 * kAttnWarps;
+#ifndef QF_ATTN_PV_BATCH
+#define QF_ATTN_PV_BATCH 8
+#endif
+constexpr int kPvBatch = QF_ATTN_PV_BATCH;  // V rows in flight per lane in PV
 
 struct AttnDev {
     const char* q;
@@ -155,8 +159,8 @@ __global__ void __launch_bounds__(kAttnThreads) paged_decode_kernel(const AttnDe
             for (int c0 = 0; c0 < NCH; c0 += 8) {
                 uint4 kv[8];
 #pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    if (c0 + c < NCH) kv[c] = ld_stream16(kr + (c0 + c) * 16);
+                for (int c = 0; c < 8; ++c)  // L1-cached: a lane's 16-byte loads share sectors
+                    if (c0 + c < NCH) kv[c] = ld_shared_ro16(kr + (c0 + c) * 16);
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
                     if (c0 + c >= NCH) break;
@@ -187,19 +191,27 @@ __global__ void __launch_bounds__(kAttnThreads) paged_decode_kernel(const AttnDe
         }
         __syncwarp();
 
-        // PV: lane = D/32 output elements; each valid key's V row, coalesced
+        // PV: lane = D/32 output elements; V rows coalesced, kPvBatch keys' loads
+        // in flight at a time.  A key that is not valid has p = 0 and reads a
+        // safe row (offset 0 of the cache), so the loop has no branch.
         const int nk = min(32, k_end - j0);
-        for (int jj = 0; jj < nk; ++jj) {
-            const int64_t off = __shfl_sync(0xffffffffu, row_off, jj);
-            const bool ok = __shfl_sync(0xffffffffu, (int)valid, jj) != 0;
-            if (!ok) continue;
-            float v[PER];
-            load_row_slice<T, PER>(a.vc + (off + lane * PER) * ES, v);
+        for (int jb = 0; jb < nk; jb += kPvBatch) {
+            float v[kPvBatch][PER];
 #pragma unroll
-            for (int h = 0; h < G; ++h) {
-                const float pj = ps[warp][h][jj];
+            for (int u = 0; u < kPvBatch; ++u) {
+                const int jj = jb + u < nk ? jb + u : nk - 1;
+                const int64_t off = __shfl_sync(0xffffffffu, row_off, jj);
+                load_row_slice<T, PER>(a.vc + (off + lane * PER) * ES, v[u]);
+            }
 #pragma unroll
-                for (int e = 0; e < PER; ++e) acc[h][e] = fmaf(pj, v[e], acc[h][e]);
+            for (int u = 0; u < kPvBatch; ++u) {
+                if (jb + u >= nk) break;
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    const float pj = ps[warp][h][jb + u];
+#pragma unroll
+                    for (int e = 0; e < PER; ++e) acc[h][e] = fmaf(pj, v[u][e], acc[h][e]);
+                }
             }
         }
         __syncwarp();
@@ -266,6 +278,320 @@ __global__ void __launch_bounds__(128) paged_decode_merge_kernel(const AttnDev a
     }
 }
 
+// ---------------------------------------------------------------------------
+// 16-bit path on the tensor cores.  Same work split (CTA = sequence, kv head,
+// partition; warps take tiles in turn) with a 16-key tile per warp step:
+//  * the tile's K and V rows are copied into the warp's own shared-memory
+//    double buffer with cp.async (16 bytes per lane, the next tile in flight
+//    while the current one is computed), chunk index XOR-swizzled by row so
+//    ldmatrix reads are free of bank conflicts;
+//  * S = Q K^T on mma.sync m16n8k16 (bf16/f16 in, fp32 accumulate): the G
+//    query heads are the M rows (padded to 16), keys the N columns;
+//  * online softmax in fp32 on the accumulator fragments (each row's values
+//    live in one quad of lanes);
+//  * O += P V on mma.sync, with P split into a 16-bit high part and the
+//    16-bit rounding of its remainder (P = hi + lo to ~16 significant bits,
+//    so the product keeps fp32-class accuracy), V fragments by ldmatrix.trans.
+template <typename T>
+struct Mma;
+
+template <>
+struct Mma<__nv_bfloat16> {
+    __device__ __forceinline__ static void run(float* c, const uint32_t* a, uint32_t b0,
+                                               uint32_t b1) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, "
+            "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+};
+
+template <>
+struct Mma<__half> {
+    __device__ __forceinline__ static void run(float* c, const uint32_t* a, uint32_t b0,
+                                               uint32_t b1) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, "
+            "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t* r, const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t* r, const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
+}
+
+// 16-byte global -> shared copy; bytes = 0 writes zeros (a key outside the
+// sequence), without reading the source.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int D>
+struct MmaTile {
+    static constexpr int TK = 16;            // keys per warp step
+    static constexpr int NCH = D * 2 / 16;   // 16-byte chunks per row
+    static constexpr int ROW = D * 2;        // bytes per row
+    static constexpr int MAT = TK * ROW;     // bytes of one K or V tile
+    static constexpr int STAGE = 2 * MAT;    // K and V
+    static constexpr int WARP = 2 * STAGE;   // double buffer
+    static constexpr int QS = 16 * ROW;      // Q (16 rows, rows >= G zero)
+    static constexpr int SMEM = QS + kAttnWarps * WARP;
+    // byte offset of logical 16-byte chunk c of row r in a swizzled tile
+    __device__ __forceinline__ static int off(int r, int c) { return r * ROW + ((c ^ (r & 7)) << 4); }
+};
+
+template <typename T, int D, int G>
+__global__ void __launch_bounds__(kAttnThreads) paged_decode_mma_kernel(const AttnDev a) {
+    using MT = MmaTile<D>;
+    using P = Packed<T>;
+    constexpr int TK = MT::TK, NCH = MT::NCH, NT = D / 8, KS = D / 16;
+    const int p = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
+    const int L = __ldg(a.lens + s);
+    const int k_begin = p * a.part;
+    if (p > 0 && k_begin >= L) return;
+    const int k_end = min(L, k_begin + a.part);
+    const int nparts = L > a.part ? (L + a.part - 1) / a.part : 1;
+
+    extern __shared__ __align__(128) unsigned char smem[];
+    unsigned char* qsm = smem;  // [16][D] T, unswizzled
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    unsigned char* wbuf = smem + MT::QS + warp * MT::WARP;
+
+    for (int i = tid; i < 16 * D; i += kAttnThreads) {
+        const int r = i / D, d = i - r * D;
+        T v = Dt<T>::from_f(0.f);
+        if (r < G)
+            v = reinterpret_cast<const T*>(a.q)[(int64_t)s * a.qs + (int64_t)(g * G + r) * a.qh + d];
+        reinterpret_cast<T*>(qsm)[i] = v;
+    }
+    __syncthreads();
+
+    const int gid = lane >> 2, tig = lane & 3;
+    uint32_t qa[KS][4];  // Q A-fragments, one per 16-dim k-step
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+        const int r = ((lane >> 3) & 1) * 8 + (lane & 7), c = 2 * ks + (lane >> 4);
+        ldsm_x4(qa[ks], qsm + r * MT::ROW + c * 16);
+    }
+
+    float o[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // rows gid, gid + 8
+    const int32_t* bt = a.bt + (int64_t)s * a.bts;
+
+    // issue the cp.async copies of the tile starting at key j0 into buffer b;
+    // returns the tile's valid-key mask (bit k: key j0 + k is read)
+    auto issue = [&](int j0, int b) -> unsigned {
+        int64_t row_off = 0;
+        bool valid = false;
+        if (lane < TK && j0 + lane < k_end) {
+            const int j = j0 + lane;
+            const int64_t lb = j / a.B;
+            const int64_t blk = __ldg(bt + lb);
+            if (blk < 0 || blk >= a.N) {
+                flag(a.status, QF_FLAG_BAD_BLOCK);
+            } else {
+                valid = true;
+                row_off = blk * a.c0 + (int64_t)g * a.c1 + (j - lb * a.B) * a.c2;
+            }
+        }
+        const unsigned mask = __ballot_sync(0xffffffffu, valid);
+        unsigned char* kt = wbuf + b * MT::STAGE;
+        unsigned char* vt = kt + MT::MAT;
+#pragma unroll
+        for (int i = lane; i < TK * NCH; i += 32) {
+            const int k = i / NCH, c = i - k * NCH;
+            const int64_t off = __shfl_sync(0xffffffffu, row_off, k);
+            const int bytes = (mask >> k) & 1 ? 16 : 0;
+            cp_async16(kt + MT::off(k, c), a.kc + off * 2 + c * 16, bytes);
+            cp_async16(vt + MT::off(k, c), a.vc + off * 2 + c * 16, bytes);
+        }
+        return mask;
+    };
+
+    int j0 = k_begin + warp * TK;
+    unsigned mask_cur = j0 < k_end ? issue(j0, 0) : 0u;
+    cp_async_commit();
+    for (int it = 0; j0 < k_end; ++it, j0 += kAttnWarps * TK) {
+        const int jn = j0 + kAttnWarps * TK;
+        const unsigned mask_next = jn < k_end ? issue(jn, (it + 1) & 1) : 0u;
+        cp_async_commit();
+        cp_async_wait<1>();  // this tile has landed (the next may still be in flight)
+        __syncwarp();
+        const unsigned char* kt = wbuf + (it & 1) * MT::STAGE;
+        const unsigned char* vt = kt + MT::MAT;
+
+        // S = Q K^T for the 16 keys (two n-tiles of 8)
+        float sc[2][4];
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+            sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+#pragma unroll
+            for (int kk = 0; kk < KS / 2; ++kk) {
+                uint32_t b[4];
+                ldsm_x4(b, kt + MT::off(n * 8 + (lane & 7), kk * 4 + (lane >> 3)));
+                Mma<T>::run(sc[n], qa[2 * kk], b[0], b[1]);
+                Mma<T>::run(sc[n], qa[2 * kk + 1], b[2], b[3]);
+            }
+        }
+        // online softmax: row gid holds sc[n][0..1], row gid + 8 holds sc[n][2..3]
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const bool ok = (mask_cur >> (n * 8 + 2 * tig + e)) & 1;
+                sc[n][e] = ok ? sc[n][e] * a.scale : -INFINITY;
+                sc[n][2 + e] = ok ? sc[n][2 + e] * a.scale : -INFINITY;
+                mx0 = fmaxf(mx0, sc[n][e]);
+                mx1 = fmaxf(mx1, sc[n][2 + e]);
+            }
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float cr0 = exp_rel(m0, mn0), cr1 = exp_rel(m1, mn1);
+        float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                sc[n][e] = exp_rel(sc[n][e], mn0);
+                sc[n][2 + e] = exp_rel(sc[n][2 + e], mn1);
+                sum0 += sc[n][e];
+                sum1 += sc[n][2 + e];
+            }
+        }
+        sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
+        sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
+        sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
+        sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
+        l0 = l0 * cr0 + sum0;
+        l1 = l1 * cr1 + sum1;
+        m0 = mn0;
+        m1 = mn1;
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            o[n][0] *= cr0;
+            o[n][1] *= cr0;
+            o[n][2] *= cr1;
+            o[n][3] *= cr1;
+        }
+        // P as A-fragments (C layout of the two n-tiles = A layout of k16), hi + lo
+        uint32_t ph[4], pl[4];
+        {
+            const float* f[4] = {&sc[0][0], &sc[0][2], &sc[1][0], &sc[1][2]};
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                ph[r] = P::pack(f[r][0], f[r][1]);
+                pl[r] = P::pack(f[r][0] - P::lo(ph[r]), f[r][1] - P::hi(ph[r]));
+            }
+        }
+        // O += P V, two output n-tiles per ldmatrix.x4.trans
+#pragma unroll
+        for (int np = 0; np < NT / 2; ++np) {
+            uint32_t b[4];
+            ldsm_x4_t(b, vt + MT::off(((lane >> 3) & 1) * 8 + (lane & 7), 2 * np + (lane >> 4)));
+            Mma<T>::run(o[2 * np], ph, b[0], b[1]);
+            Mma<T>::run(o[2 * np], pl, b[0], b[1]);
+            Mma<T>::run(o[2 * np + 1], ph, b[2], b[3]);
+            Mma<T>::run(o[2 * np + 1], pl, b[2], b[3]);
+        }
+        __syncwarp();  // every lane is done with this buffer before it is refilled
+        mask_cur = mask_next;
+    }
+    cp_async_wait<0>();
+    __syncthreads();  // all warps done: the tile buffers become the merge area
+
+    // merge the warps (rows r < G only; row gid's values: o[n][0..1], m0, l0)
+    float* wm_ = reinterpret_cast<float*>(smem + MT::QS);   // [warps][G]
+    float* wl_ = wm_ + kAttnWarps * G;                        // [warps][G]
+    float* wacc_ = wl_ + kAttnWarps * G;                      // [warps][G][D]
+    if (gid < G) {
+        if (tig == 0) {
+            wm_[warp * G + gid] = m0;
+            wl_[warp * G + gid] = l0;
+        }
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            float* dst = wacc_ + (warp * G + gid) * D + n * 8 + 2 * tig;
+            dst[0] = o[n][0];
+            dst[1] = o[n][1];
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < G * D; i += kAttnThreads) {
+        const int h = i / D, d = i - h * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm_[w * G + h]);
+        float Ls = 0.f, A = 0.f;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) {
+            const float f = exp_rel(wm_[w * G + h], M);
+            Ls += wl_[w * G + h] * f;
+            A += wacc_[(w * G + h) * D + d] * f;
+        }
+        const int hq = g * G + h;
+        if (nparts == 1) {
+            T* out = reinterpret_cast<T*>(a.out) + (int64_t)s * a.os + (int64_t)hq * a.oh;
+            out[d] = Dt<T>::from_f(A / Ls);
+        } else {
+            float* w = a.ws + (((int64_t)s * a.Hq + hq) * a.P + p) * (D + 2);
+            w[d] = A;
+            if (d == 0) {
+                w[D] = M;
+                w[D + 1] = Ls;
+            }
+        }
+    }
+}
+
+template <typename T, int D, int G>
+int launch_attn_mma(const AttnDev& a, cudaStream_t stream) {
+    constexpr auto kernel = paged_decode_mma_kernel<T, D, G>;
+    constexpr int smem = MmaTile<D>::SMEM;
+    static_assert(MmaTile<D>::QS + 2 * kAttnWarps * G * 4 + kAttnWarps * G * D * 4 <= smem,
+                  "merge area must fit in the tile buffers");
+    static std::atomic<bool> configured{false};
+    if (!configured.load(std::memory_order_relaxed)) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return launch_failed(e);
+        configured.store(true, std::memory_order_relaxed);
+    }
+    const dim3 grid((unsigned)a.P, (unsigned)a.Hkv, (unsigned)a.S);
+    kernel<<<grid, kAttnThreads, smem, stream>>>(a);
+    int rc = check_launch();
+    if (rc || a.P == 1) return rc;
+    paged_decode_merge_kernel<T, D><<<dim3((unsigned)a.Hq, (unsigned)a.S), 128, 0, stream>>>(a);
+    return check_launch();
+}
+
 template <typename T, int D, int G>
 int launch_attn(const AttnDev& a, cudaStream_t stream) {
     const dim3 grid((unsigned)a.P, (unsigned)a.Hkv, (unsigned)a.S);
@@ -276,13 +602,21 @@ int launch_attn(const AttnDev& a, cudaStream_t stream) {
     return check_launch();
 }
 
+template <typename T, int D, int G>
+int launch_best(const AttnDev& a, cudaStream_t stream) {
+#ifndef QF_ATTN_NO_MMA
+    if constexpr (sizeof(T) == 2) return launch_attn_mma<T, D, G>(a, stream);
+#endif
+    return launch_attn<T, D, G>(a, stream);
+}
+
 template <typename T, int D>
 int dispatch_g(const AttnDev& a, int G, cudaStream_t stream) {
     switch (G) {
-    case 1: return launch_attn<T, D, 1>(a, stream);
-    case 2: return launch_attn<T, D, 2>(a, stream);
-    case 4: return launch_attn<T, D, 4>(a, stream);
-    case 8: return launch_attn<T, D, 8>(a, stream);
+    case 1: return launch_best<T, D, 1>(a, stream);
+    case 2: return launch_best<T, D, 2>(a, stream);
+    case 4: return launch_best<T, D, 4>(a, stream);
+    case 8: return launch_best<T, D, 8>(a, stream);
     default: return QF_ERR_UNSUPPORTED;
     }
 }
