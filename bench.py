@@ -577,7 +577,7 @@ def run_attention(args, rank: int, world: int, local_rank: int) -> dict | None:
         "roofline": {"bound": "hbm", "kernel": "paged_decode_mma_kernel + merge",
                      "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(gbs / peak, 4), "algorithmic_bytes_per_launch": nbytes,
-                     "traffic": None},
+                     "traffic": ncu_traffic("paged_attention")},
         "gpu_launches": 2 * args.steps, "clocks": clocks,
     }
 

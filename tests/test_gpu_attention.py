@@ -133,6 +133,8 @@ def test_workspace_too_small_is_rejected():
     with pytest.raises(ValueError):
         tsb.paged_attention_forward(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), 16,
                                     sl.to(DEV), workspace=ws)
-    # (num_seqs * Hq * partitions * (head_dim + 2)) fp32 values, 512-key partitions
-    assert tsb.paged_attention_workspace_bytes(1, 8, 128, 1300) == 1 * 8 * 3 * 130 * 4
-    assert tsb.paged_attention_workspace_bytes(1, 8, 128, 512) == 0  # nothing to split
+    # (num_seqs * Hq * partitions * (head_dim + 2)) fp32 values; one sequence
+    # splits into the shortest (256-key) partitions, a large batch into 2048-key ones
+    assert tsb.paged_attention_workspace_bytes(1, 8, 128, 1300) == 1 * 8 * 6 * 130 * 4
+    assert tsb.paged_attention_workspace_bytes(1, 8, 128, 256) == 0  # nothing to split
+    assert tsb.paged_attention_workspace_bytes(512, 32, 128, 8192) == 512 * 32 * 4 * 130 * 4

@@ -95,8 +95,9 @@ def test_module_level_install_matches_stock(stock):
     _close(got, expected, "module-level install")
 
 
+@pytest.mark.parametrize("decode", ["sdpa-from-cache", "fused-kernel"])
 @pytest.mark.parametrize("block_size", [16, 4])
-def test_paged_prefill_then_decode_matches_stock(stock, block_size):
+def test_paged_prefill_then_decode_matches_stock(stock, block_size, decode):
     lens = [37, 64]
     num_blocks = 128
     blocks_each = (max(lens) + 1 + block_size - 1) // block_size
@@ -106,7 +107,9 @@ def test_paged_prefill_then_decode_matches_stock(stock, block_size):
     pool.normal_()  # poisoned: rows the batch does not write must stay as they are
     poisoned = pool.clone()
     ctx = Context()
-    patches.install_fused(fused, context=lambda: ctx, attention=CacheSdpa())
+    backend = CacheSdpa() if decode == "sdpa-from-cache" else \
+        patches.FusedDecodeAttention(prefill=CacheSdpa())
+    patches.install_fused(fused, context=lambda: ctx, attention=backend)
 
     g = torch.Generator().manual_seed(5)
     seqs = [torch.randint(0, 512, (n,), generator=g).to(DEV) for n in lens]

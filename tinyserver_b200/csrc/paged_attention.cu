@@ -25,10 +25,18 @@
 
 #include "qf_common.cuh"
 
-// Keys per CTA when a workspace allows splitting a sequence (compile-time knob).
+// Keys per CTA when a workspace allows splitting a sequence: the longest
+// partition (fewest partials, best on B200 at the c3 decode shape) unless the
+// batch has too few sequences to fill the GPU that way; then it halves, down
+// to the shortest, until there are at least kAttnTargetParts
+// (sequence, partition) pairs.  Compile-time knobs.
 #ifndef QF_ATTN_PARTITION
-#define QF_ATTN_PARTITION 512
+#define QF_ATTN_PARTITION 2048
 #endif
+#ifndef QF_ATTN_MIN_PARTITION
+#define QF_ATTN_MIN_PARTITION 256
+#endif
+constexpr int64_t kAttnTargetParts = 512;
 
 namespace qf {
 namespace {
@@ -635,13 +643,20 @@ int partitions(int64_t max_seq_len, int64_t part) {
     return (int)std::max<int64_t>(1, ceil_div(max_seq_len, part));
 }
 
+int64_t partition_keys(int64_t num_seqs, int64_t max_seq_len) {
+    int64_t part = QF_ATTN_PARTITION;
+    while (part > QF_ATTN_MIN_PARTITION && num_seqs * partitions(max_seq_len, part) < kAttnTargetParts)
+        part /= 2;
+    return part;
+}
+
 }  // namespace
 }  // namespace qf
 
 extern "C" size_t qf_paged_attention_workspace_bytes(int64_t num_seqs, int64_t num_q_heads,
                                                      int64_t head_dim, int64_t max_seq_len) {
     if (num_seqs <= 0 || num_q_heads <= 0 || head_dim <= 0 || max_seq_len <= 0) return 0;
-    const int64_t P = qf::partitions(max_seq_len, QF_ATTN_PARTITION);
+    const int64_t P = qf::partitions(max_seq_len, qf::partition_keys(num_seqs, max_seq_len));
     if (P == 1) return 0;
     return (size_t)(num_seqs * num_q_heads * P * (head_dim + 2) * (int64_t)sizeof(float));
 }
@@ -693,7 +708,7 @@ extern "C" int qf_paged_attention_decode(const qf_paged_attention_args* p, cudaS
     const int64_t need = (int64_t)qf_paged_attention_workspace_bytes(g.num_seqs, g.num_q_heads,
                                                                      D, max_len);
     if (need > 0 && g.workspace && g.workspace_bytes >= need) {
-        a.part = QF_ATTN_PARTITION;
+        a.part = (int)qf::partition_keys(g.num_seqs, max_len);
         a.P = qf::partitions(max_len, a.part);
         a.ws = static_cast<float*>(g.workspace);
     } else if (need > 0 && g.workspace) {

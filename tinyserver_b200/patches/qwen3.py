@@ -22,8 +22,9 @@ scheduler call into libqwen3fused without a change:
   ``store_kv_cache``; qwen3.py:254-357) becomes ONE
   :func:`~tinyserver_b200.qk_norm_rope_store` launch per layer, with the
   block/slot mapping built on the device once per forward and shared by all
-  layers; the attention itself stays the reference's (its varlen prefill and
-  paged decode kernels), or any backend passed in.
+  layers; decode attention runs on this library's paged attention kernel
+  (the reference's paged_attention_forward contract, paged_attention.py:
+  124-192) and prefill on the reference's varlen kernel, or any backend passed in.
 * :func:`install_operator_overrides` rebinds the module-level names the
   reference imports (``apply_rotary_pos_emb`` in modeling_qwen3 and in
   server.model.patches.qwen3, ``store_kv_cache`` / ``store_kv_cache_batched``
@@ -45,7 +46,8 @@ import torch
 from ..kernels import fused as F
 from ..kernels import kv_cache as KV
 
-__all__ = ["AttentionBackend", "ReferenceAttention", "install_fused", "fused_qwen3_model_loader",
+__all__ = ["AttentionBackend", "FusedDecodeAttention", "ReferenceAttention", "install_fused",
+           "fused_qwen3_model_loader",
            "install_operator_overrides", "restore_operator_overrides", "allocate_kv_cache",
            "batch_mapping"]
 
@@ -190,6 +192,28 @@ class ReferenceAttention:
         return out.reshape(q.shape[0], -1)
 
 
+class FusedDecodeAttention:
+    """Decode steps on this library's paged attention kernel
+    (:func:`~tinyserver_b200.paged_attention_forward`, the reference's
+    paged_attention_forward contract), prefill on ``prefill`` (default: the
+    reference's varlen kernel, loaded on first use)."""
+
+    def __init__(self, prefill: AttentionBackend | None = None):
+        self._prefill = prefill
+
+    def prefill(self, q, k, v, batch, attn):
+        if self._prefill is None:
+            self._prefill = ReferenceAttention()
+        return self._prefill.prefill(q, k, v, batch, attn)
+
+    def decode(self, q, batch, attn):
+        from ..kernels.attention import paged_attention_forward
+
+        out = paged_attention_forward(q, attn.k_cache, attn.v_cache, batch.block_tables,
+                                      attn.k_cache.shape[2], batch.seq_lens)
+        return out.reshape(q.shape[0], -1)
+
+
 @dataclass
 class BatchMapping:
     """Per-forward index data, built once and shared by every layer."""
@@ -309,8 +333,9 @@ def install_fused(model: torch.nn.Module, *, paged: bool | None = None,
     ``paged`` (default: whether the layers carry ``k_cache``/``v_cache``)
     also replaces each attention forward with the fused paged one, which reads
     the batch layout from ``context()`` (default: the reference's
-    ``get_inference_context``) and runs ``attention`` (default: the
-    reference's kernels) after the fused store."""
+    ``get_inference_context``) and runs ``attention`` after the fused store
+    (default: decode on this library's paged attention kernel, prefill on the
+    reference's varlen kernel)."""
     from transformers.models.qwen3.modeling_qwen3 import (Qwen3DecoderLayer, Qwen3MLP,
                                                           Qwen3RMSNorm)
 
@@ -334,7 +359,7 @@ def install_fused(model: torch.nn.Module, *, paged: bool | None = None,
         paged = all(hasattr(layer.self_attn, "k_cache") for layer in base.layers)
     if paged:
         ctx = context or _reference_context()
-        backend = attention or ReferenceAttention()
+        backend = attention or FusedDecodeAttention()
         inv_freq = base.rotary_emb.inv_freq
         for layer in base.layers:
             attn = layer.self_attn
