@@ -266,6 +266,34 @@ int qf_paged_attention_decode_noalloc(const qf_paged_attention_args* args, cudaS
 size_t qf_paged_attention_noalloc_capacity(void);
 
 /* ---------------------------------------------------------------------- */
+/* Prefill attention over variable-length packed sequences.  Replaces
+ * flash_attn_varlen_func (server/model/kernels/varlen_attention.py:145-218;
+ * Triton kernel :8-142): sequence b owns query rows [cu_seqlens_q[b],
+ * cu_seqlens_q[b+1]) and key/value rows [cu_seqlens_k[b], cu_seqlens_k[b+1]);
+ *   out[t, h] = softmax(q[t, h] . K_b^T * scale, causal: key j <= query i
+ *               within the sequence) @ V_b,   kv head h / (Hq / Hkv)
+ * fp32 math; for 16-bit types the probabilities are rounded to the value
+ * dtype before the product with V, as the reference does.  q, out: (Tq, Hq,
+ * D); k, v: (Tk, Hkv, D); token and head strides, head_dim contiguous, rows
+ * 16-byte aligned; cu_seqlens int32 (batch + 1); head_dim 64 or 128. */
+typedef struct {
+    const void* q; int64_t q_stride_token, q_stride_head;
+    const void* k; int64_t k_stride_token, k_stride_head;
+    const void* v; int64_t v_stride_token, v_stride_head;
+    void* out; int64_t out_stride_token, out_stride_head;
+    const int32_t* cu_seqlens_q; const int32_t* cu_seqlens_k;
+    int64_t batch, max_seqlen_q, num_q_heads, num_kv_heads, head_dim;
+    int causal;
+    float scale;
+    int dtype;
+} qf_varlen_attention_args;
+
+int qf_varlen_attention(const qf_varlen_attention_args* args, cudaStream_t stream);
+
+/* sizeof(qf_varlen_attention_args) as compiled into the library. */
+size_t qf_varlen_attention_args_size(void);
+
+/* ---------------------------------------------------------------------- */
 /* Status word: copy *status_dev to *flags_out (host) after the work queued
  * on `stream` so far, then zero it when `clear` is set.  Synchronises
  * `stream`.  Returns QF_ERR_DEVICE when any flag was set. */

@@ -18,6 +18,9 @@ reference path (citations are in the C source):
 * :func:`silu_and_mul`    -- ``Qwen3MLP`` activation product (HF:81-83)
 * :func:`paged_attention_decode` -- the reference's decode paged attention
   (server/model/kernels/paged_attention.py:8-192), in torch fp32 on the CPU
+* :func:`varlen_attention` -- the reference's prefill varlen attention
+  (server/model/kernels/varlen_attention.py:8-218), same blocking and
+  rounding points, in torch on the CPU
 """
 
 from __future__ import annotations
@@ -265,4 +268,52 @@ def paged_attention_decode(query: torch.Tensor, k_cache: torch.Tensor, v_cache: 
         q = query[s].float().view(Hkv, G, D)
         w = torch.softmax(torch.einsum("hgd,hkd->hgk", q, K) * scale, dim=-1)
         out[s] = torch.einsum("hgk,hkd->hgd", w, V).reshape(Hq, D).to(query.dtype)
+    return out
+
+
+def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                     cu_seqlens_q: torch.Tensor, cu_seqlens_k: torch.Tensor, causal: bool,
+                     softmax_scale: float | None = None, block_n: int = 32) -> torch.Tensor:
+    """Prefill attention as the reference's Triton kernel computes it
+    (server/model/kernels/varlen_attention.py:8-142): per sequence and query
+    head, keys in blocks of ``block_n`` (BLOCK_N = 32, :190), fp32 scores
+    scaled and masked (key beyond the sequence, or past the query when
+    causal, :110-115), online softmax with the running row max, and the
+    probabilities cast to the value dtype before the product with V (:121);
+    the output cast to q's dtype.  The causal loop stops at the end of the
+    query's 32-row block (:86-89), which never drops a key the mask keeps."""
+    import math
+
+    q, k, v = _cpu(q), _cpu(k), _cpu(v)
+    cq, ck = _cpu(cu_seqlens_q).tolist(), _cpu(cu_seqlens_k).tolist()
+    Tq, Hq, D = q.shape
+    Hkv = k.shape[1]
+    G = Hq // Hkv
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
+    out = torch.empty_like(q)
+    for b in range(len(cq) - 1):
+        q0, q1, k0, k1 = cq[b], cq[b + 1], ck[b], ck[b + 1]
+        nq, nk = q1 - q0, k1 - k0
+        for h in range(Hq):
+            Q = q[q0:q1, h].float()
+            K = k[k0:k1, h // G].float()
+            V = v[k0:k1, h // G]
+            m = torch.full((nq,), float("-inf"))
+            l = torch.zeros(nq)
+            acc = torch.zeros(nq, D)
+            qi = torch.arange(nq)
+            for j0 in range(0, nk, block_n):
+                kj = torch.arange(j0, min(nk, j0 + block_n))
+                s = (Q @ K[kj].T) * scale
+                if causal:
+                    s = torch.where(qi[:, None] >= kj[None, :], s, float("-inf"))
+                mn = torch.maximum(m, s.max(dim=1).values)
+                p = torch.exp(s - mn[:, None])
+                p = torch.where(torch.isnan(p), torch.zeros_like(p), p)
+                corr = torch.exp(m - mn)
+                corr = torch.where(torch.isnan(corr), torch.zeros_like(corr), corr)
+                acc = acc * corr[:, None] + p.to(v.dtype).float() @ V[kj].float()
+                l = l * corr + p.sum(dim=1)
+                m = mn
+            out[q0:q1, h] = (acc / l[:, None]).to(q.dtype)
     return out

@@ -31,6 +31,9 @@ What produces the golden outputs:
 * ``paged_attention.pt`` -- the reference's decode paged-attention Triton
   kernel (server/model/kernels/paged_attention.py) on its own tests'
   configurations plus bf16 GQA cases longer than one partition.
+* ``varlen_attention.pt`` -- the reference's prefill varlen attention kernel
+  (server/model/kernels/varlen_attention.py), causal and not, MHA and GQA,
+  fp32 (the interpreter cannot run it in bf16).
 """
 
 from __future__ import annotations
@@ -364,6 +367,36 @@ def _paged_attention_case() -> dict:
     return {"cases": cases}
 
 
+def _varlen_attention_case() -> dict:
+    """The reference's prefill varlen attention Triton kernel
+    (server/model/kernels/varlen_attention.py:145-218) under Triton's
+    interpreter: causal and non-causal, MHA and GQA, ragged packed lengths,
+    fp32 only.  Triton's interpreter cannot run this kernel in bf16 (its
+    bf16 tl.dot returned values of order 1e8 for unit-variance inputs), so
+    the bf16 rounding points -- p cast to the value dtype (:121), the final
+    store -- are restated in the oracle from the source and the fp32 cases
+    pin everything else."""
+    from server.model.kernels.varlen_attention import flash_attn_varlen_func
+
+    gen = torch.Generator().manual_seed(4242)
+    cases = []
+    for name, lens, hq, hkv, hd, causal, dt in (
+            ("mha-causal-d64", [5, 3, 7], 4, 4, 64, True, torch.float32),
+            ("gqa-causal-ragged", [1, 33, 64, 100], 8, 2, 128, True, torch.float32),
+            ("mha-noncausal", [17, 40], 8, 8, 128, False, torch.float32),
+            ("c1-lengths", [37, 64, 128, 255], 4, 2, 64, True, torch.float32)):
+        T = sum(lens)
+        q = torch.randn(T, hq, hd, generator=gen).to(dt)
+        k = torch.randn(T, hkv, hd, generator=gen).to(dt)
+        v = torch.randn(T, hkv, hd, generator=gen).to(dt)
+        cu = torch.zeros(len(lens) + 1, dtype=torch.int32)
+        cu[1:] = torch.cumsum(torch.tensor(lens), 0)
+        out = flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), causal=causal)
+        cases.append({"name": name, "q": q, "k": k, "v": v, "cu_seqlens": cu,
+                      "max_seqlen": max(lens), "causal": causal, "out": out})
+    return {"cases": cases}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("TINYSERVER_REF", "/root/reference"))
@@ -377,6 +410,10 @@ def main() -> None:
         torch.save({**_paged_attention_case(), "meta": meta},
                    os.path.join(HERE, "paged_attention.pt"))
         return
+    if args.only == "varlen_attention":
+        torch.save({**_varlen_attention_case(), "meta": meta},
+                   os.path.join(HERE, "varlen_attention.pt"))
+        return
     for dt, lens, seed, vocab, nblk, fname in (
             (torch.bfloat16, [5, 16, 37], 1234, 128, 8, "layer_bf16.pt"),
             (torch.float32, [3, 17], 1235, 128, 4, "layer_f32.pt")):
@@ -387,6 +424,8 @@ def main() -> None:
     torch.save({**_rope_case(), "meta": meta}, os.path.join(HERE, "rope_cos_sin.pt"))
     torch.save({**_outlier_case(), "meta": meta}, os.path.join(HERE, "outliers.pt"))
     torch.save({**_paged_attention_case(), "meta": meta}, os.path.join(HERE, "paged_attention.pt"))
+    torch.save({**_varlen_attention_case(), "meta": meta},
+               os.path.join(HERE, "varlen_attention.pt"))
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".pt"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

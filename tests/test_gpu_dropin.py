@@ -95,7 +95,7 @@ def test_module_level_install_matches_stock(stock):
     _close(got, expected, "module-level install")
 
 
-@pytest.mark.parametrize("decode", ["sdpa-from-cache", "fused-kernel"])
+@pytest.mark.parametrize("decode", ["sdpa-from-cache", "fused-kernel", "fused-prefill-and-decode"])
 @pytest.mark.parametrize("block_size", [16, 4])
 def test_paged_prefill_then_decode_matches_stock(stock, block_size, decode):
     lens = [37, 64]
@@ -107,8 +107,9 @@ def test_paged_prefill_then_decode_matches_stock(stock, block_size, decode):
     pool.normal_()  # poisoned: rows the batch does not write must stay as they are
     poisoned = pool.clone()
     ctx = Context()
-    backend = CacheSdpa() if decode == "sdpa-from-cache" else \
-        patches.FusedDecodeAttention(prefill=CacheSdpa())
+    backend = {"sdpa-from-cache": CacheSdpa(),
+               "fused-kernel": patches.FusedDecodeAttention(prefill=CacheSdpa()),
+               "fused-prefill-and-decode": patches.FusedDecodeAttention()}[decode]
     patches.install_fused(fused, context=lambda: ctx, attention=backend)
 
     g = torch.Generator().manual_seed(5)

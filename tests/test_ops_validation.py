@@ -110,3 +110,16 @@ def test_paged_attention_rejects_cpu_tensors():
         paged_attention_forward(torch.zeros(1, 4, 64), k_cache, torch.zeros_like(k_cache),
                                 torch.zeros(1, 1, dtype=torch.int32), 16,
                                 torch.ones(1, dtype=torch.int32))
+
+
+def test_varlen_attention_rejects_a_2d_input():
+    """Same guard as the reference (varlen_attention.py:171-172)."""
+    from tinyserver_b200 import flash_attn_varlen_func
+
+    cu = torch.tensor([0, 4], dtype=torch.int32)
+    with pytest.raises(ValueError, match="3D"):
+        flash_attn_varlen_func(torch.zeros(4, 64), torch.zeros(4, 1, 64), torch.zeros(4, 1, 64),
+                               cu, cu, 4, 4, True)
+    with pytest.raises(ValueError, match="divisible"):
+        flash_attn_varlen_func(torch.zeros(4, 3, 64), torch.zeros(4, 2, 64),
+                               torch.zeros(4, 2, 64), cu, cu, 4, 4, True)

@@ -215,3 +215,14 @@ def test_paged_attention_decode_matches_reference_kernel():
                 c["block_tables"], c["block_size"], c["seq_lens"])
             torch.testing.assert_close(out32, c["out_f32"], atol=1e-5, rtol=1e-5, msg=c["name"])
         assert torch.isfinite(out).all(), c["name"]
+
+
+def test_varlen_attention_matches_reference_kernel():
+    """The oracle against the reference's own Triton prefill attention, run
+    under Triton's interpreter, in fp32 (see make_golden.py for why bf16 is
+    not in the fixture)."""
+    g = load_golden("varlen_attention.pt")
+    for c in g["cases"]:
+        out = oracle.varlen_attention(c["q"], c["k"], c["v"], c["cu_seqlens"], c["cu_seqlens"],
+                                      c["causal"])
+        torch.testing.assert_close(out, c["out"], atol=1e-5, rtol=1e-5, msg=c["name"])

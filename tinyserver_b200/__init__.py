@@ -10,14 +10,16 @@ raises otherwise; there is no CPU fallback.
 from ._capi import lib as load_library, lib_path
 from ._runtime import check_errors
 from . import patches
-from .kernels import (apply_rotary_pos_emb, build_slot_mapping, embedding, fused_add_rms_norm,
+from .kernels import (apply_rotary_pos_emb, build_slot_mapping, embedding, flash_attn_varlen_func,
+                      fused_add_rms_norm,
                       paged_attention_forward, paged_attention_workspace_bytes,
                       qk_norm_rope_store, rms_norm, rope_cos_sin, rope_inv_freq, silu_and_mul,
                       store_kv_cache, store_kv_cache_batched)
 
 __version__ = "0.1.0"
 
-__all__ = ["apply_rotary_pos_emb", "build_slot_mapping", "check_errors", "embedding", "patches",
+__all__ = ["apply_rotary_pos_emb", "build_slot_mapping", "check_errors", "embedding",
+           "flash_attn_varlen_func", "patches",
            "fused_add_rms_norm", "load_library", "lib_path", "paged_attention_forward",
            "paged_attention_workspace_bytes", "qk_norm_rope_store", "rms_norm",
            "rope_cos_sin", "rope_inv_freq", "silu_and_mul", "store_kv_cache",

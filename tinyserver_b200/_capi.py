@@ -74,6 +74,23 @@ class PagedAttentionArgs(ctypes.Structure):
     ]
 
 
+class VarlenAttentionArgs(ctypes.Structure):
+    """Mirror of qf_varlen_attention_args (field order and types must match)."""
+
+    _fields_ = [
+        ("q", c_vp), ("q_stride_token", c_i64), ("q_stride_head", c_i64),
+        ("k", c_vp), ("k_stride_token", c_i64), ("k_stride_head", c_i64),
+        ("v", c_vp), ("v_stride_token", c_i64), ("v_stride_head", c_i64),
+        ("out", c_vp), ("out_stride_token", c_i64), ("out_stride_head", c_i64),
+        ("cu_seqlens_q", c_vp), ("cu_seqlens_k", c_vp),
+        ("batch", c_i64), ("max_seqlen_q", c_i64), ("num_q_heads", c_i64),
+        ("num_kv_heads", c_i64), ("head_dim", c_i64),
+        ("causal", c_int),
+        ("scale", c_float),
+        ("dtype", c_int),
+    ]
+
+
 # name -> argtypes of every exported entry point (restype int unless listed below)
 SIGNATURES: dict[str, list] = {
     "qf_kv_store_batched": [c_vp, I64P, c_vp, I64P, c_vp, I64P, c_vp, I64P, c_vp, c_vp, c_int,
@@ -96,6 +113,8 @@ SIGNATURES: dict[str, list] = {
     "qf_paged_attention_args_size": [],
     "qf_paged_attention_decode_noalloc": [ctypes.POINTER(PagedAttentionArgs), c_vp],
     "qf_paged_attention_noalloc_capacity": [],
+    "qf_varlen_attention": [ctypes.POINTER(VarlenAttentionArgs), c_vp],
+    "qf_varlen_attention_args_size": [],
     "qf_read_status": [c_vp, ctypes.POINTER(ctypes.c_int32), c_int, c_vp],
     "qf_last_cuda_error": [],
     "qf_version": [],
@@ -104,7 +123,8 @@ RESTYPES = {"qf_last_cuda_error": ctypes.c_char_p, "qf_version": ctypes.c_char_p
             "qf_qk_norm_rope_args_size": ctypes.c_size_t,
             "qf_paged_attention_args_size": ctypes.c_size_t,
             "qf_paged_attention_workspace_bytes": ctypes.c_size_t,
-            "qf_paged_attention_noalloc_capacity": ctypes.c_size_t}
+            "qf_paged_attention_noalloc_capacity": ctypes.c_size_t,
+            "qf_varlen_attention_args_size": ctypes.c_size_t}
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
@@ -154,7 +174,8 @@ def lib() -> ctypes.CDLL:
                 fn.argtypes = argtypes
                 fn.restype = RESTYPES.get(name, c_int)
             for fn, mirror in (("qf_qk_norm_rope_args_size", QkNormRopeArgs),
-                               ("qf_paged_attention_args_size", PagedAttentionArgs)):
+                               ("qf_paged_attention_args_size", PagedAttentionArgs),
+                               ("qf_varlen_attention_args_size", VarlenAttentionArgs)):
                 size = getattr(handle, fn)()
                 if size != ctypes.sizeof(mirror):
                     raise RuntimeError(f"{fn}: ABI mismatch, library {size} bytes, binding "

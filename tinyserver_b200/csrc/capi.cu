@@ -50,4 +50,6 @@ extern "C" size_t qf_qk_norm_rope_args_size(void) { return sizeof(qf_qk_norm_rop
 
 extern "C" size_t qf_paged_attention_args_size(void) { return sizeof(qf_paged_attention_args); }
 
+extern "C" size_t qf_varlen_attention_args_size(void) { return sizeof(qf_varlen_attention_args); }
+
 extern "C" const char* qf_version(void) { return "qwen3fused 0.1.0 sm_100a"; }

@@ -24,6 +24,7 @@
 #include <math.h>
 
 #include "qf_common.cuh"
+#include "qf_mma.cuh"
 
 // Keys per CTA when a workspace allows splitting a sequence: the longest
 // partition (fewest partials, best on B200 at the c3 decode shape) unless the
@@ -67,22 +68,6 @@ struct AttnDev {
     int part;   // keys per partition
     int32_t* status;
 };
-
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
-// exp(x - m) that is 0 when m is -inf (no key seen yet) instead of NaN.
-__device__ __forceinline__ float exp_rel(float x, float m) {
-    return m == -INFINITY ? 0.f : __expf(x - m);
-}
 
 // Load PER elements of one row (PER * sizeof(T) bytes: 4, 8 or a multiple of
 // 16) as floats.
@@ -300,61 +285,6 @@ __global__ void __launch_bounds__(128) paged_decode_merge_kernel(const AttnDev a
 //  * O += P V on mma.sync, with P split into a 16-bit high part and the
 //    16-bit rounding of its remainder (P = hi + lo to ~16 significant bits,
 //    so the product keeps fp32-class accuracy), V fragments by ldmatrix.trans.
-template <typename T>
-struct Mma;
-
-template <>
-struct Mma<__nv_bfloat16> {
-    __device__ __forceinline__ static void run(float* c, const uint32_t* a, uint32_t b0,
-                                               uint32_t b1) {
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, "
-            "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-    }
-};
-
-template <>
-struct Mma<__half> {
-    __device__ __forceinline__ static void run(float* c, const uint32_t* a, uint32_t b0,
-                                               uint32_t b1) {
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, "
-            "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-    }
-};
-
-__device__ __forceinline__ void ldsm_x4(uint32_t* r, const void* p) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
-}
-
-__device__ __forceinline__ void ldsm_x4_t(uint32_t* r, const void* p) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
-}
-
-// 16-byte global -> shared copy; bytes = 0 writes zeros (a key outside the
-// sequence), without reading the source.
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, int bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
-                     static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
-                 "l"(src), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-    asm volatile("cp.async.commit_group;" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 template <int D>
 struct MmaTile {
     static constexpr int TK = 16;            // keys per warp step

@@ -1,5 +1,6 @@
-"""Decode paged attention over the (num_blocks, num_kv_heads, block_size,
-head_dim) KV pages the fused store writes (CUDA only, no fallback).
+"""Attention on B200 (CUDA only, no fallback): decode paged attention over
+the (num_blocks, num_kv_heads, block_size, head_dim) KV pages the fused store
+writes, and prefill attention over packed variable-length sequences.
 
 :func:`paged_attention_forward` has the signature and contract of the
 reference's ``paged_attention_forward`` (server/model/kernels/
@@ -17,7 +18,7 @@ import torch
 from .. import _capi
 from .._runtime import after_op, dtype_tag, require_cuda, status_word, stream_ptr
 
-__all__ = ["paged_attention_forward", "paged_attention_workspace_bytes"]
+__all__ = ["flash_attn_varlen_func", "paged_attention_forward", "paged_attention_workspace_bytes"]
 
 
 def paged_attention_workspace_bytes(num_seqs: int, num_q_heads: int, head_dim: int,
@@ -89,4 +90,48 @@ def paged_attention_forward(query: torch.Tensor, k_cache: torch.Tensor, v_cache:
     rc = _capi.lib().qf_paged_attention_decode(a, stream_ptr(dev))
     _capi.check(rc, "paged_attention_forward")
     after_op(dev)
+    return out
+
+
+def flash_attn_varlen_func(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                           cu_seqlens_q: torch.Tensor, cu_seqlens_k: torch.Tensor,
+                           max_seqlen_q: int, max_seqlen_k: int, causal: bool,
+                           softmax_scale: float | None = None) -> torch.Tensor:
+    """Prefill attention over packed variable-length sequences, with the
+    signature and contract of the reference's ``flash_attn_varlen_func``
+    (server/model/kernels/varlen_attention.py:145-218): q (Tq, Hq, D), k/v
+    (Tk, Hkv, D), sequence b at rows [cu_seqlens[b], cu_seqlens[b+1]), GQA
+    heads grouped contiguously, causal masking within each sequence, scale
+    1/sqrt(D) unless given.  Returns a new tensor shaped like q."""
+    if q.dim() != 3 or k.dim() != 3 or v.dim() != 3:
+        raise ValueError("q, k, v must be 3D tensors")
+    Tq, Hq, D = q.shape
+    Tk, Hkv, Dk = k.shape
+    if Hq % Hkv != 0:
+        raise ValueError("num_heads_q must be divisible by num_heads_k for GQA")
+    if v.shape != k.shape or Dk != D:
+        raise ValueError(f"k {tuple(k.shape)} / v {tuple(v.shape)} do not match q {tuple(q.shape)}")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise ValueError("q, k and v must share a dtype")
+    if cu_seqlens_q.shape != cu_seqlens_k.shape or cu_seqlens_q.dim() != 1:
+        raise ValueError("cu_seqlens_q and cu_seqlens_k must be (batch + 1,)")
+    tag = dtype_tag(q, "flash_attn_varlen_func")
+    dev = require_cuda("flash_attn_varlen_func", q, k, v, cu_seqlens_q, cu_seqlens_k)
+    qq, kk, vv = (t if t.stride(2) == 1 else t.contiguous() for t in (q, k, v))
+    cq = cu_seqlens_q.to(torch.int32).contiguous()
+    ck = cu_seqlens_k.to(torch.int32).contiguous()
+    out = torch.empty_like(qq)
+    a = _capi.VarlenAttentionArgs()
+    a.q, a.q_stride_token, a.q_stride_head = qq.data_ptr(), qq.stride(0), qq.stride(1)
+    a.k, a.k_stride_token, a.k_stride_head = kk.data_ptr(), kk.stride(0), kk.stride(1)
+    a.v, a.v_stride_token, a.v_stride_head = vv.data_ptr(), vv.stride(0), vv.stride(1)
+    a.out, a.out_stride_token, a.out_stride_head = out.data_ptr(), out.stride(0), out.stride(1)
+    a.cu_seqlens_q, a.cu_seqlens_k = cq.data_ptr(), ck.data_ptr()
+    a.batch, a.max_seqlen_q = cq.numel() - 1, int(max_seqlen_q)
+    a.num_q_heads, a.num_kv_heads, a.head_dim = Hq, Hkv, D
+    a.causal = 1 if causal else 0
+    a.scale = float(softmax_scale) if softmax_scale is not None else 1.0 / math.sqrt(D)
+    a.dtype = tag
+    rc = _capi.lib().qf_varlen_attention(a, stream_ptr(dev))
+    _capi.check(rc, "flash_attn_varlen_func")
     return out

@@ -22,9 +22,9 @@ scheduler call into libqwen3fused without a change:
   ``store_kv_cache``; qwen3.py:254-357) becomes ONE
   :func:`~tinyserver_b200.qk_norm_rope_store` launch per layer, with the
   block/slot mapping built on the device once per forward and shared by all
-  layers; decode attention runs on this library's paged attention kernel
-  (the reference's paged_attention_forward contract, paged_attention.py:
-  124-192) and prefill on the reference's varlen kernel, or any backend passed in.
+  layers; attention runs on this library's kernels with the reference's
+  contracts -- paged decode (paged_attention.py:124-192) and varlen prefill
+  (varlen_attention.py:145-218) -- or on any backend passed in.
 * :func:`install_operator_overrides` rebinds the module-level names the
   reference imports (``apply_rotary_pos_emb`` in modeling_qwen3 and in
   server.model.patches.qwen3, ``store_kv_cache`` / ``store_kv_cache_batched``
@@ -195,16 +195,24 @@ class ReferenceAttention:
 class FusedDecodeAttention:
     """Decode steps on this library's paged attention kernel
     (:func:`~tinyserver_b200.paged_attention_forward`, the reference's
-    paged_attention_forward contract), prefill on ``prefill`` (default: the
-    reference's varlen kernel, loaded on first use)."""
+    paged_attention_forward contract); prefill on ``prefill`` when given,
+    else on this library's varlen kernel
+    (:func:`~tinyserver_b200.flash_attn_varlen_func`, the reference's
+    flash_attn_varlen_func contract)."""
 
     def __init__(self, prefill: AttentionBackend | None = None):
         self._prefill = prefill
 
     def prefill(self, q, k, v, batch, attn):
-        if self._prefill is None:
-            self._prefill = ReferenceAttention()
-        return self._prefill.prefill(q, k, v, batch, attn)
+        if self._prefill is not None:
+            return self._prefill.prefill(q, k, v, batch, attn)
+        from ..kernels.attention import flash_attn_varlen_func
+
+        D = q.shape[-1]
+        out = flash_attn_varlen_func(q, k, v, batch.cu_seqlens, batch.cu_seqlens,
+                                     batch.max_seqlen, batch.max_seqlen, causal=True,
+                                     softmax_scale=D ** -0.5)
+        return out.reshape(q.shape[0], -1)
 
     def decode(self, q, batch, attn):
         from ..kernels.attention import paged_attention_forward
@@ -334,8 +342,7 @@ def install_fused(model: torch.nn.Module, *, paged: bool | None = None,
     also replaces each attention forward with the fused paged one, which reads
     the batch layout from ``context()`` (default: the reference's
     ``get_inference_context``) and runs ``attention`` after the fused store
-    (default: decode on this library's paged attention kernel, prefill on the
-    reference's varlen kernel)."""
+    (default: this library's paged decode and varlen prefill kernels)."""
     from transformers.models.qwen3.modeling_qwen3 import (Qwen3DecoderLayer, Qwen3MLP,
                                                           Qwen3RMSNorm)
 
