@@ -582,6 +582,82 @@ def run_attention(args, rank: int, world: int, local_rank: int) -> dict | None:
     }
 
 
+def tensor_peak() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
+
+
+def run_prefill(args, rank: int, world: int, local_rank: int) -> dict | None:
+    """--workload prefill: causal varlen prefill attention on config c2: 16
+    packed sequences of U[128, 2048] tokens, Qwen3-1.7B heads (16 q / 8 kv,
+    head_dim 128), bf16.  A contraction, so the roofline is the tensor-core
+    one: FLOPs = sum over sequences and query heads of 4 * D * L(L+1)/2
+    (QK^T and PV over the causal half) against the measured bf16 peak."""
+    import tinyserver_b200 as tsb
+    from tinyserver_b200 import workloads as W
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = W.CONFIGS["c2"]
+    s = cfg.shape
+    lens = [n for n, _ in W.sequences(cfg, rank)]
+    T, Hq, Hkv, D = sum(lens), s.num_q_heads, s.num_kv_heads, s.head_dim
+    g = torch.Generator(device=dev).manual_seed(W.seed_of(cfg, rank) + 9)
+    q = torch.randn(T, Hq, D, generator=g, device=dev).to(cfg.dtype)
+    k = torch.randn(T, Hkv, D, generator=g, device=dev).to(cfg.dtype)
+    v = torch.randn(T, Hkv, D, generator=g, device=dev).to(cfg.dtype)
+    cu = torch.zeros(len(lens) + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(torch.tensor(lens), 0)
+    cu = cu.to(dev)
+    L = max(lens)
+
+    def once():
+        return tsb.flash_attn_varlen_func(q, k, v, cu, cu, L, L, causal=True)
+
+    for _ in range(max(args.warmup, 3)):
+        once()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local_rank).start()
+    e0.record()
+    for _ in range(args.steps):
+        once()
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        m = torch.tensor([ms], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(m, op=torch.distributed.ReduceOp.MAX)
+        ms = float(m.item())
+    if rank != 0:
+        return None
+    flops = sum(4 * D * n * (n + 1) // 2 for n in lens) * Hq
+    per_ms = ms / args.steps
+    tf = flops / (per_ms * 1e-3) / 1e12
+    peak, kind = tensor_peak()
+    return {
+        "metric": "prefill varlen attention tokens/s and TFLOP/s per B200, Qwen3-1.7B heads",
+        "value": round(world * T / (per_ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded lengths and activations of config c2",
+        "config": {"workload": f"c2 prefill attention: {len(lens)} sequences, {T} tokens, causal",
+                   "tokens": T, "max_seqlen": L},
+        "roofline": {"bound": "tensor", "kernel": "varlen_attn_mma_kernel", "achieved": round(tf, 1),
+                     "peak": peak, "unit": "TFLOP/s", "frac": round(tf / peak, 4),
+                     "peak_source": f"{kind} bf16_tflops (cuBLAS burst)", "flops_per_launch": flops,
+                     "traffic": None},
+        "gpu_launches": args.steps, "clocks": clocks,
+    }
+
+
 # ----------------------------------------------------------------------------
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -599,8 +675,9 @@ def main() -> None:
                     help="CPU-baseline timing budget (ours arm)")
     ap.add_argument("--cpu-total", type=float, default=90.0,
                     help="total CPU time budget of the --impl reference run")
-    ap.add_argument("--workload", choices=["layer", "attn"], default="layer",
-                    help="layer: the fused-layer step (the headline); attn: decode attention")
+    ap.add_argument("--workload", choices=["layer", "attn", "prefill"], default="layer",
+                    help="layer: the fused-layer step (the headline); attn: decode attention; "
+                         "prefill: varlen prefill attention")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -620,6 +697,8 @@ def main() -> None:
     try:
         if args.workload == "attn":
             line = run_attention(args, rank, world, local_rank)
+        elif args.workload == "prefill":
+            line = run_prefill(args, rank, world, local_rank)
         else:
             line = run_ours(args, rank, world, local_rank)
     finally:

@@ -26,6 +26,8 @@ __device__ __forceinline__ float exp_rel(float x, float m) {
     return m == -INFINITY ? 0.f : __expf(x - m);
 }
 
+// mma.sync is a pure register operation, so it is not volatile: the compiler
+// may interleave independent accumulators.
 template <typename T>
 struct Mma;
 
@@ -33,7 +35,7 @@ template <>
 struct Mma<__nv_bfloat16> {
     __device__ __forceinline__ static void run(float* c, const uint32_t* a, uint32_t b0,
                                                uint32_t b1) {
-        asm volatile(
+        asm(
             "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, "
             "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
             : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -45,7 +47,7 @@ template <>
 struct Mma<__half> {
     __device__ __forceinline__ static void run(float* c, const uint32_t* a, uint32_t b0,
                                                uint32_t b1) {
-        asm volatile(
+        asm(
             "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, "
             "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
             : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])

@@ -45,14 +45,17 @@ struct VarTile {
     static constexpr int QS = BM * ROW;        // Q tile
     static constexpr int MAT = BN * ROW;       // one K or V tile
     static constexpr int STAGE = 2 * MAT;
-    static constexpr int SMEM = QS + 2 * STAGE;
+    // the Q tile lives in stage 1 until its fragments are in registers (stage
+    // 1 is first refilled after that)
+    static constexpr int SMEM = 2 * STAGE;
+    static_assert(QS <= STAGE, "Q tile must fit in one stage");
     __device__ __forceinline__ static int off(int r, int c) {
         return r * ROW + ((c ^ (r & 7)) << 4);
     }
 };
 
 template <typename T, int D>
-__global__ void __launch_bounds__(128) varlen_attn_mma_kernel(const VarlenDev a) {
+__global__ void __launch_bounds__(128, 3) varlen_attn_mma_kernel(const VarlenDev a) {
     using VT = VarTile<D>;
     using P = Packed<T>;
     constexpr int BM = VT::BM, BN = VT::BN, NCH = VT::NCH, KS = D / 16, NT = D / 8;
@@ -63,8 +66,8 @@ __global__ void __launch_bounds__(128) varlen_attn_mma_kernel(const VarlenDev a)
     if (qb * BM >= q_len) return;
 
     extern __shared__ __align__(128) unsigned char smem[];
-    unsigned char* qs = smem;
-    unsigned char* stages = smem + VT::QS;
+    unsigned char* stages = smem;
+    unsigned char* qs = smem + VT::STAGE;  // stage 1
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int gid = lane >> 2, tig = lane & 3;
 
@@ -105,6 +108,7 @@ __global__ void __launch_bounds__(128) varlen_attn_mma_kernel(const VarlenDev a)
         const int r = warp * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
         ldsm_x4(qa[ks], qs + VT::off(r, 2 * ks + (lane >> 4)));
     }
+    __syncthreads();  // every warp holds its Q fragments: stage 1 may be refilled
 
     float o[NT][4];
 #pragma unroll
@@ -120,21 +124,35 @@ __global__ void __launch_bounds__(128) varlen_attn_mma_kernel(const VarlenDev a)
         const unsigned char* kt = stages + (kb & 1) * VT::STAGE;
         const unsigned char* vt = kt + VT::MAT;
 
+        // S = Q K^T: k-steps outer, the 8 key n-tiles inner, so consecutive
+        // mma.sync instructions write different accumulators
         float sc[BN / 8][4];
 #pragma unroll
-        for (int n = 0; n < BN / 8; ++n) {
-            sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+        for (int n = 0; n < BN / 8; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
 #pragma unroll
-            for (int kk = 0; kk < KS / 2; ++kk) {
-                uint32_t bf[4];
-                ldsm_x4(bf, kt + VT::off(n * 8 + (lane & 7), kk * 4 + (lane >> 3)));
-                Mma<T>::run(sc[n], qa[2 * kk], bf[0], bf[1]);
-                Mma<T>::run(sc[n], qa[2 * kk + 1], bf[2], bf[3]);
-            }
+        for (int kk = 0; kk < KS / 2; ++kk) {
+            uint32_t bf[BN / 8][4];
+#pragma unroll
+            for (int n = 0; n < BN / 8; ++n)
+                ldsm_x4(bf[n], kt + VT::off(n * 8 + (lane & 7), kk * 4 + (lane >> 3)));
+#pragma unroll
+            for (int n = 0; n < BN / 8; ++n) Mma<T>::run(sc[n], qa[2 * kk], bf[n][0], bf[n][1]);
+#pragma unroll
+            for (int n = 0; n < BN / 8; ++n)
+                Mma<T>::run(sc[n], qa[2 * kk + 1], bf[n][2], bf[n][3]);
         }
         // Online softmax and P V in 32-key halves: the reference updates its
         // running max every BLOCK_N = 32 keys (varlen_attention.py:190) and
         // rounds P against it, so the rounding points line up.
+        // Scores are kept in log2 units (scale * log2(e) folded into one
+        // multiply) so that exp2 gives the exponentials.  Every row has a
+        // valid key in the first 32 keys (key 0), so the running max is finite
+        // from the first half on and the exponentials need no -inf guard.
+        // Masks only where this warp's rows can see a masked key: the block's
+        // tail past the sequence, or keys beyond the warp's first row (causal).
+        const float sl2 = a.scale * 1.4426950408889634f;
+        const bool full = (kb + 1) * BN <= k_len &&
+                          (!a.causal || (kb + 1) * BN <= qb * BM + warp * 16 + 1);
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
             float mx0 = -INFINITY, mx1 = -INFINITY;
@@ -142,13 +160,16 @@ __global__ void __launch_bounds__(128) varlen_attn_mma_kernel(const VarlenDev a)
             for (int n = 4 * hf; n < 4 * hf + 4; ++n) {
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                    const int kj = kb * BN + n * 8 + 2 * tig + e;
-                    const bool ok0 = kj < k_len && (!a.causal || qi0 >= kj);
-                    const bool ok1 = kj < k_len && (!a.causal || qi1 >= kj);
-                    sc[n][e] = ok0 ? sc[n][e] * a.scale : -INFINITY;
-                    sc[n][2 + e] = ok1 ? sc[n][2 + e] * a.scale : -INFINITY;
-                    mx0 = fmaxf(mx0, sc[n][e]);
-                    mx1 = fmaxf(mx1, sc[n][2 + e]);
+                    float s0 = sc[n][e] * sl2, s1 = sc[n][2 + e] * sl2;
+                    if (!full) {
+                        const int kj = kb * BN + n * 8 + 2 * tig + e;
+                        s0 = kj < k_len && (!a.causal || qi0 >= kj) ? s0 : -INFINITY;
+                        s1 = kj < k_len && (!a.causal || qi1 >= kj) ? s1 : -INFINITY;
+                    }
+                    sc[n][e] = s0;
+                    sc[n][2 + e] = s1;
+                    mx0 = fmaxf(mx0, s0);
+                    mx1 = fmaxf(mx1, s1);
                 }
             }
             mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
@@ -156,13 +177,13 @@ __global__ void __launch_bounds__(128) varlen_attn_mma_kernel(const VarlenDev a)
             mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
             mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
             const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-            const float cr0 = exp_rel(m0, mn0), cr1 = exp_rel(m1, mn1);
+            const float cr0 = exp2f(m0 - mn0), cr1 = exp2f(m1 - mn1);  // 0 on the first half
             float sum0 = 0.f, sum1 = 0.f;
             uint32_t pa[2][4];  // P rounded to T: A-fragments of this half's two k-steps
 #pragma unroll
             for (int n = 4 * hf; n < 4 * hf + 4; ++n) {
-                const float p0 = exp_rel(sc[n][0], mn0), p1 = exp_rel(sc[n][1], mn0);
-                const float p2 = exp_rel(sc[n][2], mn1), p3 = exp_rel(sc[n][3], mn1);
+                const float p0 = exp2f(sc[n][0] - mn0), p1 = exp2f(sc[n][1] - mn0);
+                const float p2 = exp2f(sc[n][2] - mn1), p3 = exp2f(sc[n][3] - mn1);
                 sum0 += p0 + p1;
                 sum1 += p2 + p3;
                 pa[(n / 2) & 1][(n & 1) * 2 + 0] = P::pack(p0, p1);
