@@ -658,6 +658,128 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> dict | None:
     }
 
 
+SAMPLE_ROWS, SAMPLE_VOCAB = 256, 151936
+
+
+def _sample_inputs(B: int, V: int, seed: int, device) -> tuple:
+    """One decode step's sampling inputs: bf16 logits N(0, 4^2) (a spread LM
+    distribution), per-row mixed settings -- 1 in 8 rows greedy, temperature
+    0.6..1.2, top-k off/20/50/1000, top-p off/0.9/0.95 -- and counter-hash
+    uniforms."""
+    g = torch.Generator().manual_seed(seed)
+    logits = (torch.randn(B, V, generator=g) * 4.0).to(torch.bfloat16)
+    pick = lambda vals: torch.tensor(vals)[torch.randint(0, len(vals), (B,), generator=g)]
+    temperature = pick([0.0, 0.6, 0.7, 0.8, 0.9, 1.0, 1.0, 1.2]).float()
+    top_k = pick([0, 0, 20, 50, 1000]).long()
+    top_p = pick([1.0, 0.9, 0.95, 0.95]).float()
+    seeds = torch.randint(0, 2 ** 62, (B,), generator=g)
+    return (logits.to(device), temperature.to(device), top_k.to(device), top_p.to(device),
+            seeds.to(device), torch.full((B,), seed, dtype=torch.int64, device=device))
+
+
+def run_sample(args, rank: int, world: int, local_rank: int) -> dict | None:
+    """--workload sample: the batched sampler after lm_head on a c3-sized
+    decode step: 256 rows of Qwen3's 151936-token vocabulary, bf16 logits,
+    mixed greedy / temperature / top-k / top-p rows, counter-hash noise fused
+    into the launch.  Three logits buffers (233 MB together, larger than L2)
+    rotate so every step reads its logits from HBM.  Roofline: HBM, on the
+    logits bytes read once per launch."""
+    import tinyserver_b200 as tsb
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    B, V = SAMPLE_ROWS, SAMPLE_VOCAB
+    sets = [_sample_inputs(B, V, 1000 * rank + i, dev) for i in range(3)]
+
+    def once(i):
+        x, t, k, p, sd, st = sets[i % 3]
+        return tsb.sample_tokens_seeded(x, t, k, p, sd, st)
+
+    for i in range(max(args.warmup, 3)):
+        once(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local_rank).start()
+    e0.record()
+    for i in range(args.steps):
+        once(i)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        m = torch.tensor([ms], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(m, op=torch.distributed.ReduceOp.MAX)
+        ms = float(m.item())
+
+    # end to end: logits from pinned host memory, tokens back to the host
+    e2e = None
+    if not args.no_e2e:
+        host = [s[0].cpu().pin_memory() for s in sets[:2]]
+        dbuf = [torch.empty_like(s[0]) for s in sets[:2]]
+        out_h = torch.empty(B, dtype=torch.int64).pin_memory()
+        n_e2e = max(10, min(args.steps, 50))
+        _, t, k, p, sd, st = sets[0]
+        for i in range(3):
+            dbuf[i % 2].copy_(host[i % 2], non_blocking=True)
+            out_h.copy_(tsb.sample_tokens_seeded(dbuf[i % 2], t, k, p, sd, st), non_blocking=True)
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for i in range(n_e2e):
+            dbuf[i % 2].copy_(host[i % 2], non_blocking=True)
+            out_h.copy_(tsb.sample_tokens_seeded(dbuf[i % 2], t, k, p, sd, st), non_blocking=True)
+        a1.record()
+        torch.cuda.synchronize()
+        e2e_ms = a0.elapsed_time(a1) / n_e2e
+        e2e = {"value": round(world * B / (e2e_ms * 1e-3), 1), "unit": "rows/s",
+               "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": B * V * 2,
+               "d2h_bytes_per_step": B * 8}
+    if rank != 0:
+        return None
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import oracle
+        x, t, k, p, sd, st = (s.cpu() for s in sets[0])
+        n = 32
+        u = oracle.uniforms_from_seeds(sd[:n].tolist(), st[:n].tolist())
+        oracle.sample_tokens(x[:4], t[:4], k[:4], p[:4], u[:4])
+        c0 = time.perf_counter()
+        reps = 0
+        while True:
+            oracle.sample_tokens(x[:n], t[:n], k[:n], p[:n], u)
+            reps += 1
+            if time.perf_counter() - c0 > min(args.cpu_seconds, 10.0):
+                break
+        cs = (time.perf_counter() - c0) / reps
+        cpu = {"value": round(n / cs, 1), "unit": "rows/s", "cores": torch.get_num_threads(),
+               "kind": "port", "sample": f"{n} rows of the same batch, {reps} repetitions, the "
+                                         "reference's sort-based sample_tokens restated in torch "
+                                         "on the host cores"}
+
+    per_ms = ms / args.steps
+    nbytes = B * V * 2 + B * (4 + 8 + 4 + 8 + 8 + 8)
+    gbs = nbytes / (per_ms * 1e-3) / 1e9
+    peak, kind = hbm_peak()
+    return {
+        "metric": "sampled rows/s per B200 (Qwen3 vocabulary, top-k/top-p/temperature mix)",
+        "value": round(world * B / (per_ms * 1e-3), 1), "unit": "rows/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded bf16 logits N(0, 16), mixed per-row sampling settings",
+        "config": {"workload": f"c3 decode step sampling: {B} rows x {V} vocab, bf16 logits",
+                   "rows": B, "vocab": V, "l2": "3 rotating logits buffers (233 MB > L2)"},
+        "roofline": {"bound": "hbm", "kernel": "sample_kernel", "achieved": round(gbs, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
+                     "peak_source": f"{kind} hbm_gbs", "bytes_per_launch": nbytes,
+                     "traffic": ncu_traffic("sample_kernel")},
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks,
+    }
+
+
 # ----------------------------------------------------------------------------
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -675,9 +797,10 @@ def main() -> None:
                     help="CPU-baseline timing budget (ours arm)")
     ap.add_argument("--cpu-total", type=float, default=90.0,
                     help="total CPU time budget of the --impl reference run")
-    ap.add_argument("--workload", choices=["layer", "attn", "prefill"], default="layer",
+    ap.add_argument("--workload", choices=["layer", "attn", "prefill", "sample"],
+                    default="layer",
                     help="layer: the fused-layer step (the headline); attn: decode attention; "
-                         "prefill: varlen prefill attention")
+                         "prefill: varlen prefill attention; sample: the batched sampler")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -699,6 +822,8 @@ def main() -> None:
             line = run_attention(args, rank, world, local_rank)
         elif args.workload == "prefill":
             line = run_prefill(args, rank, world, local_rank)
+        elif args.workload == "sample":
+            line = run_sample(args, rank, world, local_rank)
         else:
             line = run_ours(args, rank, world, local_rank)
     finally:

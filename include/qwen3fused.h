@@ -294,6 +294,48 @@ int qf_varlen_attention(const qf_varlen_attention_args* args, cudaStream_t strea
 size_t qf_varlen_attention_args_size(void);
 
 /* ---------------------------------------------------------------------- */
+/* Batched token sampling.  Replaces sample_tokens
+ * (server/model/sampling.py:118-194): per row b of logits (batch, vocab),
+ *   s = float(logits[b]) / max(temperature[b], 1e-5)
+ *   order: s descending, ties by ascending index (a stable sort)
+ *   top-k: keep the first k ranks (top_k <= 0 or >= vocab keeps all)
+ *   softmax over the kept ranks; top-p: drop every rank whose probability
+ *   mass before it exceeds top_p (rank 0 always stays)
+ *   out[b] = the first rank whose cumulative mass reaches
+ *            uniforms[b] * (kept mass), as a token id;
+ *   temperature <= 0: out[b] = argmax (lowest index among equal maxima).
+ * No sort: a radix select over the order-preserving bits of s, with the
+ * probability masses held as exact fixed-point integers.
+ * The uniforms come either from `uniforms` (float32) or, when that is NULL,
+ * from the counter hash of (seeds[b], steps[b]) that
+ * uniforms_from_seeds (server/model/determinism.py:30-73) computes on the
+ * host.  temperature, top_p: float32; top_k: int32 or int64 (top_k_type);
+ * seeds, steps: int64 (bits read as unsigned); out: int64.  logits rows are
+ * contiguous, `logits_row_stride` elements apart. */
+typedef struct {
+    const void* logits; int64_t logits_row_stride;
+    int64_t batch, vocab;
+    int dtype;
+    const float* temperature;
+    const void* top_k; int top_k_type;
+    const float* top_p;
+    const float* uniforms;
+    const int64_t* seeds; const int64_t* steps;
+    int64_t* out;
+} qf_sample_args;
+
+int qf_sample_tokens(const qf_sample_args* args, cudaStream_t stream);
+
+/* sizeof(qf_sample_args) as compiled into the library. */
+size_t qf_sample_args_size(void);
+
+/* out[i] = uniform_from_hash(seeds[i], steps[i])
+ * (server/model/determinism.py:30-51): splitmix64 of (seed, step), top 53
+ * bits scaled by 2^-53, clamped to 1 - 2^-24, rounded to float32. */
+int qf_uniforms_from_seeds(const int64_t* seeds, const int64_t* steps, int64_t n, float* out,
+                           cudaStream_t stream);
+
+/* ---------------------------------------------------------------------- */
 /* Status word: copy *status_dev to *flags_out (host) after the work queued
  * on `stream` so far, then zero it when `clear` is set.  Synchronises
  * `stream`.  Returns QF_ERR_DEVICE when any flag was set. */

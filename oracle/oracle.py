@@ -317,3 +317,106 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                 m = mn
             out[q0:q1, h] = (acc / l[:, None]).to(q.dtype)
     return out
+
+
+# ---------------------------------------------------------------------------
+# Sampling (server/model/sampling.py, server/model/determinism.py)
+
+_MASK64 = (1 << 64) - 1
+
+
+def mix64(seed: int, step: int) -> int:
+    """splitmix64 of (seed, step) (determinism.py:30-41): seed times the
+    golden-ratio increment plus step, then the two xor-shift-multiply rounds
+    and a final xor-shift, all modulo 2^64."""
+    x = ((seed & _MASK64) * 0x9E3779B97F4A7C15 + (step & _MASK64)) & _MASK64
+    x = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & _MASK64
+    x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & _MASK64
+    return x ^ (x >> 31)
+
+
+def uniform_from_hash(seed: int, step: int) -> float:
+    """Top 53 bits of mix64 scaled by 2^-53, capped at 1 - 2^-24
+    (determinism.py:44-51)."""
+    return min((mix64(seed, step) >> 11) * 2.0 ** -53, 1.0 - 2.0 ** -24)
+
+
+def uniforms_from_seeds(seeds, steps) -> torch.Tensor:
+    """float32 [B] of uniform_from_hash per row (determinism.py:54-73)."""
+    return torch.tensor([uniform_from_hash(int(s), int(t)) for s, t in zip(seeds, steps)],
+                        dtype=torch.float32)
+
+
+def sample_tokens(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
+                  top_p: torch.Tensor, uniforms: torch.Tensor) -> torch.Tensor:
+    """The reference's batched sampler (sampling.py:118-194) in torch on the
+    CPU, step for step: float32 logits over the clamped temperature, a
+    stable descending sort, top-k as -inf past rank k, softmax, top-p
+    dropping ranks whose mass before them exceeds top_p (rank 0 kept),
+    inverse-CDF pick by searchsorted of u * total, greedy rows at rank 0."""
+    logits, temperature, top_k, top_p, uniforms = (
+        _cpu(t) for t in (logits, temperature, top_k, top_p, uniforms))
+    B, V = logits.shape
+    s = logits.float() / temperature.float().clamp(min=1e-5)[:, None]
+    vals, order = torch.sort(s, dim=-1, descending=True, stable=True)
+    keep = torch.where(top_k > 0, top_k, V)[:, None]
+    vals = vals.masked_fill(torch.arange(V)[None, :] >= keep, float("-inf"))
+    p = torch.softmax(vals, dim=-1)
+    before = torch.cumsum(p, dim=-1) - p
+    drop = before > top_p[:, None]
+    drop[:, 0] = False
+    cdf = torch.cumsum(p.masked_fill(drop, 0.0), dim=-1)
+    target = (uniforms.float()[:, None] * cdf[:, -1:]).contiguous()
+    rank = torch.searchsorted(cdf.contiguous(), target).clamp(max=V - 1)
+    rank = torch.where(temperature[:, None] <= 0, torch.zeros_like(rank), rank)
+    return order.gather(-1, rank).squeeze(-1)
+
+
+def sample_margins(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
+                   top_p: torch.Tensor, uniforms: torch.Tensor):
+    """The same decisions in float64 (exact order, exp and sums in double),
+    with each row's distance from a decision boundary: the smaller of
+    |mass before the first dropped rank - top_p|, |mass before the last kept
+    rank - top_p| and the distance of u * total from the CDF values either
+    side of the pick, all as fractions of the kept mass.  A row whose margin
+    is below the float32 rounding of the reference's own softmax and cumsums
+    can legitimately land on either neighbour.  Returns (tokens, margins);
+    greedy rows get margin inf."""
+    import numpy as np
+
+    logits, temperature, top_k, top_p, uniforms = (
+        _cpu(t) for t in (logits, temperature, top_k, top_p, uniforms))
+    B, V = logits.shape
+    s32 = (logits.float() / temperature.float().clamp(min=1e-5)[:, None]).numpy()
+    toks = np.zeros(B, dtype=np.int64)
+    margins = np.full(B, np.inf)
+    for b in range(B):
+        order = np.argsort(-s32[b].astype(np.float64), kind="stable")
+        if float(temperature[b]) <= 0:
+            toks[b] = order[0]
+            continue
+        k = int(top_k[b])
+        k = k if 0 < k < V else V
+        sv = s32[b][order[:k]].astype(np.float64)
+        e = np.exp(sv - sv[0])
+        p = e / e.sum()
+        incl = np.cumsum(p)
+        before = incl - p
+        tp = float(top_p[b])
+        later = np.nonzero(before[1:] > tp)[0]
+        R = int(later[0]) + 1 if later.size else k
+        margin = np.inf
+        if tp < 1.0:  # at top_p >= 1 no rank is dropped in exact arithmetic
+            if R < k:
+                margin = min(margin, before[R] - tp)
+            if R > 1:
+                margin = min(margin, tp - before[R - 1])
+        cdf = incl[:R]
+        target = float(uniforms[b]) * cdf[-1]
+        r = int(np.searchsorted(cdf, target, side="left"))
+        r = min(r, R - 1)
+        lo = cdf[r - 1] if r > 0 else 0.0
+        margin = min(margin, target - lo if r > 0 else np.inf, cdf[r] - target)
+        toks[b] = order[r]
+        margins[b] = margin
+    return torch.from_numpy(toks), torch.from_numpy(margins)

@@ -34,6 +34,9 @@ What produces the golden outputs:
 * ``varlen_attention.pt`` -- the reference's prefill varlen attention kernel
   (server/model/kernels/varlen_attention.py), causal and not, MHA and GQA,
   fp32 (the interpreter cannot run it in bf16).
+* ``sampling.pt`` -- the reference's batched sampler and counter-based noise
+  (server/model/sampling.py, server/model/determinism.py) on hand-checkable
+  rows, Qwen3-vocabulary bf16 rows, tie-heavy fp32 rows and fp16 extremes.
 """
 
 from __future__ import annotations
@@ -397,6 +400,80 @@ def _varlen_attention_case() -> dict:
     return {"cases": cases}
 
 
+def _sampling_case() -> dict:
+    """The reference's batched sampler (server/model/sampling.py:118-194) and
+    its counter-based noise (server/model/determinism.py:30-73), run as
+    shipped on the CPU:
+
+    * small hand-checkable rows in the spirit of the reference's own tests
+      (tests/model/test_batch_sampling.py): equal logits, a greedy tie, per-row
+      top-k 1/2/3, a tiny top-p, top-k above the vocabulary, u = 0 and u near 1;
+    * bf16 rows at Qwen3's vocabulary (151936) with mixed temperature / top-k /
+      top-p and uniforms from the hash;
+    * fp32 integer-valued logits (long runs of equal values, where the stable
+      sort's index order decides) with -inf entries;
+    * fp16 rows with top_p 0, top_k 1, extreme temperatures;
+    * uniform_from_hash at edge seeds and steps.
+    """
+    from server.model.determinism import mix64, uniform_from_hash, uniforms_from_seeds
+    from server.model.sampling import sample_tokens
+
+    gen = torch.Generator().manual_seed(77)
+    cases = []
+
+    def add(name, logits, temperature, top_k, top_p, uniforms):
+        out = sample_tokens(logits, temperature, top_k, top_p, uniforms)
+        cases.append({"name": name, "logits": logits, "temperature": temperature,
+                      "top_k": top_k, "top_p": top_p, "uniforms": uniforms, "out": out})
+
+    f32, i64 = torch.float32, torch.int64
+    row = [5.0, 4.0, 3.0, 2.0, 1.0, 0.0]
+    small = torch.tensor([[0.0, 0.0, 0.0, 0.0, 0.0, 0.0]] * 4 + [[0.0, 5.0, 5.0, 1.0, 0.0, 0.0]]
+                         + [row] * 3 + [[-10.0, -10.0, 10.0, -10.0, -10.0, -10.0]] * 2
+                         + [[1.0, 9.0, 3.0, 7.0, 2.0, 0.5]] * 2, dtype=f32)
+    add("hand", small,
+        torch.tensor([1.0] * 4 + [0.0] + [1.0] * 7, dtype=f32),
+        torch.tensor([0] * 5 + [1, 2, 3] + [0, 999, 0, 0], dtype=i64),
+        torch.tensor([1.0] * 8 + [1e-6, 1.0, 1.0, 0.5], dtype=f32),
+        torch.tensor([0.1, 0.4, 0.6, 0.9, 0.99, 0.999, 0.999, 0.999, 0.9, 0.3, 0.0,
+                      1.0 - 2.0 ** -24], dtype=f32))
+
+    B, V = 8, 151936
+    logits = (torch.randn(B, V, generator=gen) * 3.0).to(torch.bfloat16)
+    add("bf16-qwen3-vocab", logits,
+        torch.tensor([0.0, 0.6, 0.8, 1.0, 1.0, 0.7, 1.2, 0.9], dtype=f32),
+        torch.tensor([0, 0, 50, 0, 20, 1000, 0, 40], dtype=i64),
+        torch.tensor([1.0, 0.9, 0.95, 1.0, 0.8, 0.9, 0.6, 1.0], dtype=f32),
+        uniforms_from_seeds(list(range(100, 100 + B)), [7] * B))
+
+    B, V = 64, 4096
+    logits = torch.randint(-8, 9, (B, V), generator=gen).to(f32)
+    logits[::5, ::7] = float("-inf")
+    add("f32-ties", logits,
+        torch.tensor([0.5, 1.0, 2.0, 0.0] * 16, dtype=f32),
+        torch.tensor([0, 7, 100, 0, 4095, 4096, 1, 300] * 8, dtype=i64),
+        torch.tensor([1.0, 0.9, 0.3, 0.99, 0.5, 1.0, 0.7, 0.05] * 8, dtype=f32),
+        uniforms_from_seeds([s * 7919 for s in range(B)], list(range(B))))
+
+    B, V = 16, 32000
+    logits = (torch.randn(B, V, generator=gen) * 2.0).to(torch.float16)
+    add("f16-extremes", logits,
+        torch.tensor([1e-6, 50.0, 1.0, 1.0] * 4, dtype=f32),
+        torch.tensor([0, 0, 1, 5] * 4, dtype=i64),
+        torch.tensor([0.9, 0.95, 1.0, 0.0] * 4, dtype=f32),
+        uniforms_from_seeds([2 ** 64 - 1 - s for s in range(B)], [10 ** 6] * B))
+
+    seeds = [0, 1, 2, 42, 1234, 2 ** 31, 2 ** 63, 2 ** 64 - 1]
+    steps = [0, 1, 9, 10_000, 2 ** 40]
+    pairs = [(sd, st) for sd in seeds for st in steps]
+    hash_case = {"seeds": [p[0] for p in pairs], "steps": [p[1] for p in pairs],
+                 "mix64": [mix64(*p) for p in pairs],
+                 "uniform": [uniform_from_hash(*p) for p in pairs],
+                 "uniforms_f32": uniforms_from_seeds([p[0] for p in pairs],
+                                                     [p[1] for p in pairs])}
+    return {"cases": cases, "hash": hash_case}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("TINYSERVER_REF", "/root/reference"))
@@ -409,6 +486,9 @@ def main() -> None:
     if args.only == "paged_attention":
         torch.save({**_paged_attention_case(), "meta": meta},
                    os.path.join(HERE, "paged_attention.pt"))
+        return
+    if args.only == "sampling":
+        torch.save({**_sampling_case(), "meta": meta}, os.path.join(HERE, "sampling.pt"))
         return
     if args.only == "varlen_attention":
         torch.save({**_varlen_attention_case(), "meta": meta},
@@ -426,6 +506,7 @@ def main() -> None:
     torch.save({**_paged_attention_case(), "meta": meta}, os.path.join(HERE, "paged_attention.pt"))
     torch.save({**_varlen_attention_case(), "meta": meta},
                os.path.join(HERE, "varlen_attention.pt"))
+    torch.save({**_sampling_case(), "meta": meta}, os.path.join(HERE, "sampling.pt"))
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".pt"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

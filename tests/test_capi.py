@@ -30,7 +30,8 @@ def test_header_declares_the_expected_entry_points():
     for required in ("qf_kv_store_batched", "qf_kv_store_seq", "qf_rmsnorm", "qf_add_rmsnorm",
                      "qf_rope_cos_sin", "qf_qk_norm_rope_store", "qf_silu_and_mul",
                      "qf_embedding", "qf_build_slot_mapping", "qf_paged_attention_decode",
-                     "qf_paged_attention_workspace_bytes", "qf_read_status"):
+                     "qf_paged_attention_workspace_bytes", "qf_varlen_attention",
+                     "qf_sample_tokens", "qf_uniforms_from_seeds", "qf_read_status"):
         assert required in names
 
 
@@ -44,6 +45,9 @@ def test_library_exports_every_declared_symbol():
 def test_struct_abi_matches():
     lib = _capi.lib()
     assert lib.qf_qk_norm_rope_args_size() == ctypes.sizeof(_capi.QkNormRopeArgs)
+    assert lib.qf_paged_attention_args_size() == ctypes.sizeof(_capi.PagedAttentionArgs)
+    assert lib.qf_varlen_attention_args_size() == ctypes.sizeof(_capi.VarlenAttentionArgs)
+    assert lib.qf_sample_args_size() == ctypes.sizeof(_capi.SampleArgs)
 
 
 def test_version():
@@ -65,7 +69,16 @@ def test_host_side_argument_checks_return_before_any_launch():
     ct = _capi.i64_array([0, 0, 0, 0])
     assert lib.qf_kv_store_batched(None, st, None, st, None, ct, None, ct, None, None, 1, 4, 2,
                                    8, 2, 0, 2, None, None) == _capi.QF_ERR_INVALID
+    sa = _capi.SampleArgs()
+    sa.batch, sa.vocab, sa.dtype = 2, 0, 2
+    assert lib.qf_sample_tokens(ctypes.byref(sa), None) == _capi.QF_ERR_INVALID  # empty vocab
+    sa.vocab = 16
+    assert lib.qf_sample_tokens(ctypes.byref(sa), None) == _capi.QF_ERR_INVALID  # null pointers
+    assert lib.qf_uniforms_from_seeds(None, None, -1, None, None) == _capi.QF_ERR_INVALID
     # zero-sized work is a no-op that needs no device
+    sa.batch = 0
+    assert lib.qf_sample_tokens(ctypes.byref(sa), None) == _capi.QF_OK
+    assert lib.qf_uniforms_from_seeds(None, None, 0, None, None) == _capi.QF_OK
     assert lib.qf_silu_and_mul(None, 0, None, 0, None, 0, 0, 8, 2, None) == _capi.QF_OK
     assert lib.qf_kv_store_seq(0, None, 0, 1, None, st, None, st, None, ct, None, ct, 0, 2, 8,
                                2, 4, 2, None, None) == _capi.QF_OK

@@ -123,3 +123,30 @@ def test_varlen_attention_rejects_a_2d_input():
     with pytest.raises(ValueError, match="divisible"):
         flash_attn_varlen_func(torch.zeros(4, 3, 64), torch.zeros(4, 2, 64),
                                torch.zeros(4, 2, 64), cu, cu, 4, 4, True)
+
+
+def test_sample_tokens_rejects_bad_shapes_like_the_reference():
+    """The reference's shape errors (tests/model/test_batch_sampling.py
+    test_rejects_bad_shapes): same messages, raised before any device work."""
+    with pytest.raises(ValueError, match="Expected logits shape"):
+        tsb.sample_tokens(torch.randn(10), torch.ones(1), torch.zeros(1, dtype=torch.int64),
+                          torch.ones(1), torch.ones(1) * 0.5)
+    with pytest.raises(ValueError, match="Expected top_k shape"):
+        tsb.sample_tokens(torch.randn(2, 10), torch.ones(2), torch.zeros(3, dtype=torch.int64),
+                          torch.ones(2), torch.ones(2) * 0.5)
+    with pytest.raises(ValueError, match="Expected uniforms shape"):
+        tsb.sample_tokens(torch.randn(2, 10), torch.ones(2), torch.zeros(2, dtype=torch.int64),
+                          torch.ones(2), torch.ones(3))
+
+
+def test_sample_tokens_rejects_cpu_tensors():
+    with pytest.raises(ValueError, match="CUDA tensors only"):
+        tsb.sample_tokens(torch.randn(2, 10), torch.ones(2), torch.zeros(2, dtype=torch.int64),
+                          torch.ones(2), torch.ones(2) * 0.5)
+
+
+def test_uniforms_from_seeds_checks_lengths_and_device():
+    with pytest.raises(ValueError, match="same length"):
+        tsb.uniforms_from_seeds([1, 2, 3], [0, 1])
+    with pytest.raises(ValueError, match="CUDA tensors only"):
+        tsb.uniforms_from_seeds([1, 2], [0, 1], device="cpu")

@@ -226,3 +226,37 @@ def test_varlen_attention_matches_reference_kernel():
         out = oracle.varlen_attention(c["q"], c["k"], c["v"], c["cu_seqlens"], c["cu_seqlens"],
                                       c["causal"])
         torch.testing.assert_close(out, c["out"], atol=1e-5, rtol=1e-5, msg=c["name"])
+
+
+def test_sampler_matches_reference():
+    """The oracle's sampler against the reference's sample_tokens on every
+    fixture row: the same algorithm in torch on the CPU, so the tokens agree
+    exactly."""
+    g = load_golden("sampling.pt")
+    for c in g["cases"]:
+        out = oracle.sample_tokens(c["logits"], c["temperature"], c["top_k"], c["top_p"],
+                                   c["uniforms"])
+        assert out.dtype == torch.int64
+        assert out.tolist() == c["out"].tolist(), c["name"]
+
+
+def test_sampler_float64_decisions_agree_away_from_boundaries():
+    """The float64 restatement (used to tell which rows sit on a decision
+    boundary) picks the reference's token on every row whose margin is above
+    the float32 rounding of the reference's softmax and cumsums."""
+    g = load_golden("sampling.pt")
+    for c in g["cases"]:
+        toks, margins = oracle.sample_margins(c["logits"], c["temperature"], c["top_k"],
+                                              c["top_p"], c["uniforms"])
+        clear = margins > 1e-6
+        assert clear.float().mean() > 0.75, c["name"]
+        assert toks[clear].tolist() == c["out"][clear].tolist(), c["name"]
+
+
+def test_counter_hash_matches_reference():
+    h = load_golden("sampling.pt")["hash"]
+    for sd, st, m, u in zip(h["seeds"], h["steps"], h["mix64"], h["uniform"]):
+        assert oracle.mix64(sd, st) == m
+        assert oracle.uniform_from_hash(sd, st) == u
+        assert 0.0 <= u < 1.0
+    assert torch.equal(oracle.uniforms_from_seeds(h["seeds"], h["steps"]), h["uniforms_f32"])

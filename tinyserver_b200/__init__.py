@@ -13,8 +13,9 @@ from . import patches
 from .kernels import (apply_rotary_pos_emb, build_slot_mapping, embedding, flash_attn_varlen_func,
                       fused_add_rms_norm,
                       paged_attention_forward, paged_attention_workspace_bytes,
-                      qk_norm_rope_store, rms_norm, rope_cos_sin, rope_inv_freq, silu_and_mul,
-                      store_kv_cache, store_kv_cache_batched)
+                      qk_norm_rope_store, rms_norm, rope_cos_sin, rope_inv_freq, sample_tokens,
+                      sample_tokens_seeded, silu_and_mul, store_kv_cache, store_kv_cache_batched,
+                      uniforms_from_seeds)
 
 __version__ = "0.1.0"
 
@@ -22,5 +23,5 @@ __all__ = ["apply_rotary_pos_emb", "build_slot_mapping", "check_errors", "embedd
            "flash_attn_varlen_func", "patches",
            "fused_add_rms_norm", "load_library", "lib_path", "paged_attention_forward",
            "paged_attention_workspace_bytes", "qk_norm_rope_store", "rms_norm",
-           "rope_cos_sin", "rope_inv_freq", "silu_and_mul", "store_kv_cache",
-           "store_kv_cache_batched"]
+           "rope_cos_sin", "rope_inv_freq", "sample_tokens", "sample_tokens_seeded",
+           "silu_and_mul", "store_kv_cache", "store_kv_cache_batched", "uniforms_from_seeds"]

@@ -91,6 +91,22 @@ class VarlenAttentionArgs(ctypes.Structure):
     ]
 
 
+class SampleArgs(ctypes.Structure):
+    """Mirror of qf_sample_args (field order and types must match)."""
+
+    _fields_ = [
+        ("logits", c_vp), ("logits_row_stride", c_i64),
+        ("batch", c_i64), ("vocab", c_i64),
+        ("dtype", c_int),
+        ("temperature", c_vp),
+        ("top_k", c_vp), ("top_k_type", c_int),
+        ("top_p", c_vp),
+        ("uniforms", c_vp),
+        ("seeds", c_vp), ("steps", c_vp),
+        ("out", c_vp),
+    ]
+
+
 # name -> argtypes of every exported entry point (restype int unless listed below)
 SIGNATURES: dict[str, list] = {
     "qf_kv_store_batched": [c_vp, I64P, c_vp, I64P, c_vp, I64P, c_vp, I64P, c_vp, c_vp, c_int,
@@ -115,6 +131,9 @@ SIGNATURES: dict[str, list] = {
     "qf_paged_attention_noalloc_capacity": [],
     "qf_varlen_attention": [ctypes.POINTER(VarlenAttentionArgs), c_vp],
     "qf_varlen_attention_args_size": [],
+    "qf_sample_tokens": [ctypes.POINTER(SampleArgs), c_vp],
+    "qf_sample_args_size": [],
+    "qf_uniforms_from_seeds": [c_vp, c_vp, c_i64, c_vp, c_vp],
     "qf_read_status": [c_vp, ctypes.POINTER(ctypes.c_int32), c_int, c_vp],
     "qf_last_cuda_error": [],
     "qf_version": [],
@@ -124,7 +143,8 @@ RESTYPES = {"qf_last_cuda_error": ctypes.c_char_p, "qf_version": ctypes.c_char_p
             "qf_paged_attention_args_size": ctypes.c_size_t,
             "qf_paged_attention_workspace_bytes": ctypes.c_size_t,
             "qf_paged_attention_noalloc_capacity": ctypes.c_size_t,
-            "qf_varlen_attention_args_size": ctypes.c_size_t}
+            "qf_varlen_attention_args_size": ctypes.c_size_t,
+            "qf_sample_args_size": ctypes.c_size_t}
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
@@ -175,7 +195,8 @@ def lib() -> ctypes.CDLL:
                 fn.restype = RESTYPES.get(name, c_int)
             for fn, mirror in (("qf_qk_norm_rope_args_size", QkNormRopeArgs),
                                ("qf_paged_attention_args_size", PagedAttentionArgs),
-                               ("qf_varlen_attention_args_size", VarlenAttentionArgs)):
+                               ("qf_varlen_attention_args_size", VarlenAttentionArgs),
+                               ("qf_sample_args_size", SampleArgs)):
                 size = getattr(handle, fn)()
                 if size != ctypes.sizeof(mirror):
                     raise RuntimeError(f"{fn}: ABI mismatch, library {size} bytes, binding "

@@ -52,4 +52,6 @@ extern "C" size_t qf_paged_attention_args_size(void) { return sizeof(qf_paged_at
 
 extern "C" size_t qf_varlen_attention_args_size(void) { return sizeof(qf_varlen_attention_args); }
 
+extern "C" size_t qf_sample_args_size(void) { return sizeof(qf_sample_args); }
+
 extern "C" const char* qf_version(void) { return "qwen3fused 0.1.0 sm_100a"; }

@@ -1,0 +1,668 @@
+// Batched token sampling without a sort.
+//
+// Replaces sample_tokens (server/model/sampling.py:118-194).  For row b:
+//   s_i = float(logits[b, i]) / max(temperature[b], 1e-5)          (:166-168)
+//   ranks: s descending, equal s by ascending index (stable sort, :172-174)
+//   top-k keeps ranks < k (k <= 0 or >= V keeps all, :178-180)
+//   p = softmax over the kept ranks (:182)
+//   top-p keeps rank r when the mass of ranks < r is <= top_p (:186-189)
+//   token = the first rank whose cumulative mass is >= u * (kept mass)
+//           (inverse-CDF pick, :193-198); temperature <= 0: the argmax (:203-205).
+//
+// Every step above is "the first rank, in (s desc, index asc) order, whose
+// cumulative weight reaches a threshold": top-k by count, top-p and the pick
+// by mass.  This kernel finds each such rank with a radix select instead of a
+// sort.  The order key of s is its float bits with the sign folded so that
+// unsigned comparison follows s; its top 11, middle 11 and low 10 bits are
+// three digit levels.  Per level, every CTA histograms its elements (count
+// and mass) by digit, the cluster adds the histograms over distributed shared
+// memory, and a descending scan finds the digit where the cumulative weight
+// crosses the threshold; the next level only counts elements under that
+// prefix.  After three levels the key is exact; elements with equal keys have
+// equal s, equal mass and consecutive ranks in index order, so the rank inside
+// that group is arithmetic, and for the pick one CTA walks its slice in index
+// order to name the token.
+//
+// Masses are exp(s - max) as fixed-point integers (x 2^40, u64): integer sums
+// do not depend on the order of addition, so the per-CTA histograms, their
+// cluster sum and every deeper level agree exactly, and the result does not
+// depend on how the vocabulary is split.  Thresholds: top-p keeps ranks up to
+// and including the first whose inclusive mass exceeds top_p * (kept mass);
+// the pick is the first rank whose inclusive mass is >= ceil(u * kept mass).
+//
+// One cluster of kClusterCtas CTAs per row; each CTA keeps its slice of the
+// row in shared memory as fp32 s, so the row is read from HBM once.
+#include <cooperative_groups.h>
+
+#include "qf_common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace qf {
+namespace {
+
+#ifndef QF_SAMPLE_CLUSTER
+#define QF_SAMPLE_CLUSTER 8
+#endif
+
+constexpr int kClusterCtas = QF_SAMPLE_CLUSTER;
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+constexpr int kBins = 2048;                     // digits per level (level 3 uses 1024)
+constexpr int kOwn = kBins / kClusterCtas;      // combined bins each CTA holds
+constexpr int kPer = kOwn / 32;                 // of those, per lane of the scanning warp
+constexpr float kMassScale = 1099511627776.0f;  // 2^40
+static_assert(kOwn <= kThreads && kOwn % 32 == 0, "cluster size must be 4..64");
+using u64 = unsigned long long;
+
+struct SampleDev {
+    const char* logits;
+    int64_t row_stride;  // elements
+    int64_t vocab;
+    int slice;           // elements per CTA, a multiple of 8
+    int vec;             // 16-byte loads (aligned rows)
+    const float* temperature;
+    const void* top_k;
+    int top_k_i64;
+    const float* top_p;
+    const float* uniforms;
+    const int64_t* seeds;
+    const int64_t* steps;
+    int64_t* out;
+};
+
+// The crossing found by a descending scan: its digit, the cumulative weight
+// of everything ranked above it, and its own weight.
+struct Crossing {
+    int found;
+    int digit;
+    u64 above_cnt, above_mas, cnt, mas;
+};
+
+struct SampleShared {
+    u64 mas[kBins];  // this CTA's histogram at the current level
+    uint32_t cnt[kBins];
+    u64 own1_mas[kOwn];  // level 1 summed over the cluster: this CTA's bin range
+    uint32_t own1_cnt[kOwn];
+    u64 own2_mas[kOwn];  // levels 2 and 3
+    uint32_t own2_cnt[kOwn];
+    u64 tot1_mas, tot2_mas;  // totals of the own ranges
+    uint32_t tot1_cnt, tot2_cnt;
+    float max_s;  // this CTA's maximum and its lowest global index
+    uint32_t max_idx;
+    u64 red_mas[kWarps];
+    uint32_t red_cnt[kWarps];
+    Crossing res;
+    float row_max;
+    uint32_t row_argmax;
+    u64 z_all;
+    int owner;
+    uint32_t owner_j;
+};
+
+__device__ __forceinline__ uint32_t order_key(float s) {
+    const uint32_t b = __float_as_uint(s);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__device__ __forceinline__ u64 mass_of(float s, float m) {
+    return __float2ull_rn(expf(s - m) * kMassScale);
+}
+
+__device__ __forceinline__ bool better(float s, uint32_t i, float t, uint32_t j) {
+    return s > t || (s == t && i < j);
+}
+
+// splitmix64 of (seed, step), top 53 bits as a double in [0, 1), clamped to
+// the largest float32 below 1 -- uniform_from_hash, determinism.py:30-51.
+__device__ __forceinline__ float uniform_from_hash(uint64_t seed, uint64_t step) {
+    uint64_t x = seed * 0x9E3779B97F4A7C15ull + step;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    x ^= x >> 31;
+    const double u = fmin((double)(x >> 11) * 0x1p-53, 1.0 - 0x1p-24);
+    return __double2float_rn(u);
+}
+
+template <typename F>
+__device__ __forceinline__ void for_each_s(const float* sv, int n, F&& f) {
+    const int n4 = n >> 2;
+    const float4* s4 = reinterpret_cast<const float4*>(sv);
+    for (int q = threadIdx.x; q < n4; q += kThreads) {
+        const float4 v = s4[q];
+        f(v.x);
+        f(v.y);
+        f(v.z);
+        f(v.w);
+    }
+    for (int i = (n4 << 2) + (int)threadIdx.x; i < n; i += kThreads) f(sv[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ float scaled(T x, float tc) {
+    const float s = __fdiv_rn(Dt<T>::to_f(x), tc);
+    return s == 0.0f ? 0.0f : s;  // -0 ranks with +0, as in the sort
+}
+
+// Load this CTA's slice, write s to shared memory, return the thread's best
+// (s, local index).
+template <typename T>
+__device__ __forceinline__ void load_slice(const SampleDev& a, const T* row, int n, float tc,
+                                           float* sv, float& best, uint32_t& best_i) {
+    if (a.vec) {
+        constexpr int PV = Dt<T>::kPerVec;
+        const int nv = n / PV;
+        for (int c = threadIdx.x; c < nv; c += kThreads) {
+            const uint4 raw = ld_stream16(row + (int64_t)c * PV);
+            const T* x = reinterpret_cast<const T*>(&raw);
+            float v[PV];
+#pragma unroll
+            for (int j = 0; j < PV; ++j) {
+                v[j] = scaled<T>(x[j], tc);
+                if (v[j] > best || best_i == 0xffffffffu) {
+                    best = v[j];
+                    best_i = (uint32_t)(c * PV + j);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < PV; j += 4)
+                *reinterpret_cast<float4*>(sv + c * PV + j) = make_float4(v[j], v[j + 1], v[j + 2],
+                                                                          v[j + 3]);
+        }
+        for (int i = nv * PV + (int)threadIdx.x; i < n; i += kThreads) {
+            const float v = scaled<T>(row[i], tc);
+            sv[i] = v;
+            if (v > best || best_i == 0xffffffffu) {
+                best = v;
+                best_i = (uint32_t)i;
+            }
+        }
+    } else {
+        for (int i = threadIdx.x; i < n; i += kThreads) {
+            const float v = scaled<T>(row[i], tc);
+            sv[i] = v;
+            if (v > best || best_i == 0xffffffffu) {
+                best = v;
+                best_i = (uint32_t)i;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void zero_hist(SampleShared& sm) {
+    for (int i = threadIdx.x; i < kBins; i += kThreads) {
+        sm.cnt[i] = 0;
+        sm.mas[i] = 0;
+    }
+}
+
+// Histogram of this CTA's elements whose key has `prefix` above bit `hi`,
+// by the digit (key >> shift) & mask.  hi == 32: no prefix.
+__device__ __forceinline__ void build_hist(SampleShared& sm, const float* sv, int n, float m,
+                                           int hi, uint32_t prefix, int shift, uint32_t mask) {
+    for_each_s(sv, n, [&](float s) {
+        const uint32_t k = order_key(s);
+        if (hi == 32 || (k >> hi) == prefix) {
+            const uint32_t d = (k >> shift) & mask;
+            atomicAdd(&sm.cnt[d], 1u);
+            const u64 w = mass_of(s, m);
+            if (w) atomicAdd(&sm.mas[d], w);
+        }
+    });
+}
+
+// Sum the cluster's histograms over this CTA's bin range into own_* and its
+// total into tot_*.  Call between two cluster barriers.
+__device__ void combine(const cg::cluster_group& cl, SampleShared& sm, u64* own_mas,
+                        uint32_t* own_cnt, u64* tot_mas, uint32_t* tot_cnt) {
+    const int rank = (int)cl.block_rank();
+    u64 m = 0;
+    uint32_t c = 0;
+    if (threadIdx.x < kOwn) {
+        const int b = rank * kOwn + threadIdx.x;
+#pragma unroll
+        for (int q = 0; q < kClusterCtas; ++q) {
+            const SampleShared* r = cl.map_shared_rank(&sm, q);
+            m += r->mas[b];
+            c += r->cnt[b];
+        }
+        own_mas[threadIdx.x] = m;
+        own_cnt[threadIdx.x] = c;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < kOwn / 32) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            m += __shfl_down_sync(0xffffffffu, m, o);
+            c += __shfl_down_sync(0xffffffffu, c, o);
+        }
+        if (lane == 0) {
+            sm.red_mas[warp] = m;
+            sm.red_cnt[warp] = c;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        u64 tm = 0;
+        uint32_t tc = 0;
+        for (int w = 0; w < kOwn / 32; ++w) {
+            tm += sm.red_mas[w];
+            tc += sm.red_cnt[w];
+        }
+        *tot_mas = tm;
+        *tot_cnt = tc;
+    }
+}
+
+__device__ __forceinline__ void scan_up(u64& c, u64& m, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const u64 xc = __shfl_up_sync(0xffffffffu, c, o);
+        const u64 xm = __shfl_up_sync(0xffffffffu, m, o);
+        if (lane >= o) {
+            c += xc;
+            m += xm;
+        }
+    }
+}
+
+// Warp 0: the first combined bin, in descending digit order, that is not empty
+// and whose inclusive cumulative weight (count or mass, starting from
+// above_*) reaches tau.  Every lane returns the same result.
+__device__ Crossing search(const cg::cluster_group& cl, SampleShared& sm, bool level1,
+                           bool by_mass, u64 tau, u64 above_cnt, u64 above_mas) {
+    const int lane = threadIdx.x & 31;
+    Crossing f{};
+    // the CTAs' ranges, highest digits (last CTA) first
+    u64 tc = 0, tm = 0;
+    if (lane < kClusterCtas) {
+        const SampleShared* r = cl.map_shared_rank(&sm, kClusterCtas - 1 - lane);
+        tc = level1 ? r->tot1_cnt : r->tot2_cnt;
+        tm = level1 ? r->tot1_mas : r->tot2_mas;
+    }
+    u64 ic = tc, im = tm;
+    scan_up(ic, im, lane);
+    bool cond = lane < kClusterCtas && tc > 0 && (by_mass ? above_mas + im : above_cnt + ic) >= tau;
+    unsigned bal = __ballot_sync(0xffffffffu, cond);
+    if (!bal) return f;
+    int L = __ffs(bal) - 1;
+    above_cnt += __shfl_sync(0xffffffffu, ic - tc, L);
+    above_mas += __shfl_sync(0xffffffffu, im - tm, L);
+    const int rho = kClusterCtas - 1 - L;
+    // that CTA's bins, descending; lane l takes kPer consecutive ones
+    const SampleShared* r = cl.map_shared_rank(&sm, rho);
+    const uint32_t* oc = level1 ? r->own1_cnt : r->own2_cnt;
+    const u64* om = level1 ? r->own1_mas : r->own2_mas;
+    uint32_t bc[kPer];
+    u64 bm[kPer];
+    u64 lc = 0, lm = 0;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int b = kOwn - 1 - (lane * kPer + i);
+        bc[i] = oc[b];
+        bm[i] = om[b];
+        lc += bc[i];
+        lm += bm[i];
+    }
+    ic = lc;
+    im = lm;
+    scan_up(ic, im, lane);
+    cond = lc > 0 && (by_mass ? above_mas + im : above_cnt + ic) >= tau;
+    bal = __ballot_sync(0xffffffffu, cond);
+    if (!bal) return f;  // unreachable: the range total crossed
+    L = __ffs(bal) - 1;
+    if (lane == L) {
+        u64 c0 = above_cnt + ic - lc, m0 = above_mas + im - lm;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            if (!f.found && bc[i] > 0 && (by_mass ? m0 + bm[i] : c0 + bc[i]) >= tau) {
+                f.found = 1;
+                f.digit = rho * kOwn + kOwn - 1 - (lane * kPer + i);
+                f.above_cnt = c0;
+                f.above_mas = m0;
+                f.cnt = bc[i];
+                f.mas = bm[i];
+            }
+            c0 += bc[i];
+            m0 += bm[i];
+        }
+    }
+    f.found = __shfl_sync(0xffffffffu, f.found, L);
+    f.digit = __shfl_sync(0xffffffffu, f.digit, L);
+    f.above_cnt = __shfl_sync(0xffffffffu, f.above_cnt, L);
+    f.above_mas = __shfl_sync(0xffffffffu, f.above_mas, L);
+    f.cnt = __shfl_sync(0xffffffffu, f.cnt, L);
+    f.mas = __shfl_sync(0xffffffffu, f.mas, L);
+    return f;
+}
+
+// Run `search` on warp 0 and hand the result to the whole CTA.
+__device__ __forceinline__ Crossing search_all(const cg::cluster_group& cl, SampleShared& sm,
+                                               bool level1, bool by_mass, u64 tau, u64 above_cnt,
+                                               u64 above_mas) {
+    __syncthreads();  // everyone has read the previous result
+    if (threadIdx.x < 32) {
+        const Crossing f = search(cl, sm, level1, by_mass, tau, above_cnt, above_mas);
+        if (threadIdx.x == 0) sm.res = f;
+    }
+    __syncthreads();
+    return sm.res;
+}
+
+// One deeper level: histogram under `prefix`, cluster sum, scan.
+__device__ __forceinline__ Crossing deeper(const cg::cluster_group& cl, SampleShared& sm,
+                                           const float* sv, int n, float m, int hi,
+                                           uint32_t prefix, int shift, uint32_t mask, bool by_mass,
+                                           u64 tau, const Crossing& parent) {
+    zero_hist(sm);
+    __syncthreads();
+    build_hist(sm, sv, n, m, hi, prefix, shift, mask);
+    cl.sync();  // every CTA's histogram is complete
+    combine(cl, sm, sm.own2_mas, sm.own2_cnt, &sm.tot2_mas, &sm.tot2_cnt);
+    cl.sync();  // every CTA's combined range is complete
+    return search_all(cl, sm, false, by_mass, tau, parent.above_cnt, parent.above_mas);
+}
+
+// The rank where the cumulative weight first reaches tau.
+struct Selected {
+    int found;
+    uint32_t key;       // order key of the rank's s
+    uint32_t low_digit; // its level-3 digit (this CTA's cnt[] holds its local count)
+    u64 j;              // position inside the group of equal keys (index order)
+    u64 incl_cnt;       // ranks up to and including it
+    u64 incl_mas;       // their mass
+};
+
+__device__ Selected select_rank(const cg::cluster_group& cl, SampleShared& sm, const float* sv,
+                                int n, float m, bool by_mass, u64 tau) {
+    Selected out{};
+    const Crossing f1 = search_all(cl, sm, true, by_mass, tau, 0, 0);
+    if (!f1.found) return out;
+    const uint32_t p1 = (uint32_t)f1.digit;
+    const Crossing f2 = deeper(cl, sm, sv, n, m, 21, p1, 10, 2047u, by_mass, tau, f1);
+    if (!f2.found) return out;
+    const uint32_t p2 = (p1 << 11) | (uint32_t)f2.digit;
+    const Crossing f3 = deeper(cl, sm, sv, n, m, 10, p2, 0, 1023u, by_mass, tau, f2);
+    if (!f3.found) return out;
+    out.found = 1;
+    out.key = (p2 << 10) | (uint32_t)f3.digit;
+    out.low_digit = (uint32_t)f3.digit;
+    const u64 w = f3.mas / f3.cnt;  // equal keys, equal masses
+    if (by_mass)
+        out.j = (w == 0 || tau <= f3.above_mas) ? 0 : (tau - f3.above_mas + w - 1) / w - 1;
+    else
+        out.j = tau - f3.above_cnt - 1;
+    out.incl_cnt = f3.above_cnt + out.j + 1;
+    out.incl_mas = f3.above_mas + (out.j + 1) * w;
+    return out;
+}
+
+// The j-th element (in index order) of this CTA's slice whose key is `key`;
+// the caller knows it exists.  Returns the local index (all threads).
+__device__ int nth_with_key(SampleShared& sm, const float* sv, int n, uint32_t key, uint32_t j) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int span = ((n + kWarps - 1) / kWarps + 31) & ~31;
+    const int lo = warp * span, hi = min(n, lo + span);
+    uint32_t c = 0;
+    for (int b = lo; b < hi; b += 32) {
+        const int i = b + lane;
+        c += __popc(__ballot_sync(0xffffffffu, i < hi && order_key(sv[i]) == key));
+    }
+    if (lane == 0) sm.red_cnt[warp] = c;
+    sm.owner = -1;
+    __syncthreads();
+    uint32_t before = 0;
+    for (int w = 0; w < warp; ++w) before += sm.red_cnt[w];
+    if (j >= before && j < before + c) {
+        uint32_t jj = j - before;
+        for (int b = lo; b < hi; b += 32) {
+            const int i = b + lane;
+            const unsigned bal = __ballot_sync(0xffffffffu, i < hi && order_key(sv[i]) == key);
+            const uint32_t pc = __popc(bal);
+            if (jj < pc) {
+                if (((bal >> lane) & 1u) && __popc(bal & ((1u << lane) - 1u)) == (int)jj)
+                    sm.owner = i;
+                break;
+            }
+            jj -= pc;
+        }
+    }
+    __syncthreads();
+    return sm.owner;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleDev a) {
+    extern __shared__ __align__(16) float sv[];
+    __shared__ SampleShared sm;
+    const cg::cluster_group cl = cg::this_cluster();
+    const int rank = (int)cl.block_rank();
+    const int64_t row = blockIdx.x / kClusterCtas;
+    const int64_t base = (int64_t)rank * a.slice;
+    const int64_t left = a.vocab - base;
+    const int n = left <= 0 ? 0 : (left < a.slice ? (int)left : a.slice);
+    const T* lrow = reinterpret_cast<const T*>(a.logits) + row * a.row_stride + base;
+
+    const float temp = a.temperature[row];
+    const float tc = fmaxf(temp, 1e-5f);
+
+    // ---- load the slice, row maximum --------------------------------------
+    float best = -INFINITY;
+    uint32_t best_i = 0xffffffffu;
+    load_slice<T>(a, lrow, n, tc, sv, best, best_i);
+    if (best_i != 0xffffffffu) best_i += (uint32_t)base;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float s2 = __shfl_down_sync(0xffffffffu, best, o);
+        const uint32_t i2 = __shfl_down_sync(0xffffffffu, best_i, o);
+        if (i2 != 0xffffffffu && (best_i == 0xffffffffu || better(s2, i2, best, best_i))) {
+            best = s2;
+            best_i = i2;
+        }
+    }
+    if (lane == 0) {
+        sm.red_mas[warp] = __float_as_uint(best);
+        sm.red_cnt[warp] = best_i;
+    }
+    zero_hist(sm);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float b = -INFINITY;
+        uint32_t bi = 0xffffffffu;
+        for (int w = 0; w < kWarps; ++w) {
+            const float s2 = __uint_as_float((uint32_t)sm.red_mas[w]);
+            const uint32_t i2 = sm.red_cnt[w];
+            if (i2 != 0xffffffffu && (bi == 0xffffffffu || better(s2, i2, b, bi))) {
+                b = s2;
+                bi = i2;
+            }
+        }
+        sm.max_s = b;
+        sm.max_idx = bi;
+    }
+    cl.sync();
+    if (threadIdx.x == 0) {
+        float b = -INFINITY;
+        uint32_t bi = 0xffffffffu;
+        for (int q = 0; q < kClusterCtas; ++q) {
+            const SampleShared* r = cl.map_shared_rank(&sm, q);
+            const float s2 = r->max_s;
+            const uint32_t i2 = r->max_idx;
+            if (i2 != 0xffffffffu && (bi == 0xffffffffu || better(s2, i2, b, bi))) {
+                b = s2;
+                bi = i2;
+            }
+        }
+        sm.row_max = b;
+        sm.row_argmax = bi;
+    }
+    __syncthreads();
+    const float m = sm.row_max;
+
+    if (temp <= 0.0f) {  // greedy: rank 0 of the stable order
+        if (rank == 0 && threadIdx.x == 0) a.out[row] = sm.row_argmax;
+        cl.sync();  // no CTA leaves while others may read its shared memory
+        return;
+    }
+
+    // ---- level 1 over the whole row: counts and masses ---------------------
+    build_hist(sm, sv, n, m, 32, 0, 21, 2047u);
+    cl.sync();
+    combine(cl, sm, sm.own1_mas, sm.own1_cnt, &sm.tot1_mas, &sm.tot1_cnt);
+    cl.sync();
+    u64 z_all = 0;
+    if (threadIdx.x == 0)
+        for (int q = 0; q < kClusterCtas; ++q) z_all += cl.map_shared_rank(&sm, q)->tot1_mas;
+    if (threadIdx.x == 0) sm.z_all = z_all;
+    __syncthreads();
+    z_all = sm.z_all;
+
+    // ---- top-k -------------------------------------------------------------
+    const int64_t V = a.vocab;
+    const int64_t k = a.top_k_i64 ? reinterpret_cast<const int64_t*>(a.top_k)[row]
+                                  : (int64_t)reinterpret_cast<const int32_t*>(a.top_k)[row];
+    const u64 k_eff = (k > 0 && k < V) ? (u64)k : (u64)V;
+    u64 z_k = z_all;
+    if (k_eff < (u64)V) {
+        const Selected c = select_rank(cl, sm, sv, n, m, false, k_eff);
+        if (c.found) z_k = c.incl_mas;
+    }
+
+    // ---- top-p -------------------------------------------------------------
+    const float top_p = a.top_p[row];
+    u64 z_r = z_k;
+    if (top_p < 1.0f) {
+        const double theta = (double)top_p * (double)z_k;
+        const u64 tau = theta < 0.0 ? 0 : (u64)floor(theta) + 1;
+        const Selected c = select_rank(cl, sm, sv, n, m, true, tau);
+        if (c.found && c.incl_cnt < k_eff) z_r = c.incl_mas;
+    }
+
+    // ---- the pick ----------------------------------------------------------
+    const float u = a.uniforms ? a.uniforms[row]
+                               : uniform_from_hash((uint64_t)a.seeds[row], (uint64_t)a.steps[row]);
+    u64 tau = (u64)ceil((double)u * (double)z_r);
+    if (tau > z_r) tau = z_r;
+    const Selected pick = select_rank(cl, sm, sv, n, m, true, tau);
+    if (pick.found) {
+        // which CTA holds the pick: prefix over the CTAs' counts of the key
+        if (threadIdx.x < 32) {
+            uint32_t c = 0;
+            if (lane < kClusterCtas) c = cl.map_shared_rank(&sm, lane)->cnt[pick.low_digit];
+            uint32_t incl = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += x;
+            }
+            const bool own = lane < kClusterCtas && pick.j >= incl - c && pick.j < incl;
+            const unsigned bal = __ballot_sync(0xffffffffu, own);
+            if (lane == 0) {
+                const int L = bal ? __ffs(bal) - 1 : -1;
+                sm.owner = L;
+                sm.owner_j = 0;
+            }
+            __syncwarp();
+            if (own) sm.owner_j = (uint32_t)(pick.j - (incl - c));
+        }
+        __syncthreads();
+        const int owner = sm.owner;
+        const uint32_t jj = sm.owner_j;
+        __syncthreads();
+        if (owner == rank) {
+            const int li = nth_with_key(sm, sv, n, pick.key, jj);
+            if (threadIdx.x == 0) a.out[row] = li >= 0 ? base + li : (int64_t)sm.row_argmax;
+        } else if (owner < 0 && rank == 0 && threadIdx.x == 0) {
+            a.out[row] = sm.row_argmax;  // unreachable: some CTA holds the pick
+        }
+    } else if (rank == 0 && threadIdx.x == 0) {
+        a.out[row] = sm.row_argmax;  // unreachable: tau <= kept mass
+    }
+    cl.sync();  // no CTA leaves while others may read its shared memory
+}
+
+__global__ void uniforms_kernel(const int64_t* seeds, const int64_t* steps, int64_t n,
+                                float* out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = uniform_from_hash((uint64_t)seeds[i], (uint64_t)steps[i]);
+}
+
+template <typename T>
+int launch_sample(const SampleDev& a, int64_t batch, cudaStream_t stream) {
+    constexpr auto kernel = sample_kernel<T>;
+    static std::atomic<int> max_dyn{-1};
+    if (max_dyn.load(std::memory_order_relaxed) < 0) {
+        int dev = 0, optin = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        const int dyn = optin - (int)sizeof(SampleShared) - 1024;
+        const cudaError_t e =
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
+        if (e != cudaSuccess) return launch_failed(e);
+        max_dyn.store(dyn, std::memory_order_relaxed);
+    }
+    const size_t smem = (size_t)a.slice * sizeof(float);
+    if ((int64_t)smem > max_dyn.load(std::memory_order_relaxed)) return QF_ERR_UNSUPPORTED;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(batch * kClusterCtas));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kClusterCtas;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, a);
+    return e == cudaSuccess ? QF_OK : launch_failed(e);
+}
+
+}  // namespace
+}  // namespace qf
+
+extern "C" int qf_sample_tokens(const qf_sample_args* p, cudaStream_t stream) {
+    if (!p) return QF_ERR_INVALID;
+    const qf_sample_args& g = *p;
+    if (g.batch < 0 || g.vocab <= 0) return QF_ERR_INVALID;
+    if (g.batch == 0) return QF_OK;
+    if (!g.logits || !g.temperature || !g.top_k || !g.top_p || !g.out) return QF_ERR_INVALID;
+    if (!g.uniforms && (!g.seeds || !g.steps)) return QF_ERR_INVALID;
+    if (g.dtype != QF_F32 && g.dtype != QF_F16 && g.dtype != QF_BF16) return QF_ERR_INVALID;
+    if (g.top_k_type != QF_I32 && g.top_k_type != QF_I64) return QF_ERR_INVALID;
+    if (g.logits_row_stride < g.vocab && g.batch > 1) return QF_ERR_INVALID;
+    if (g.vocab >= (int64_t)1 << 31 || g.batch > (int64_t)1 << 24) return QF_ERR_UNSUPPORTED;
+    const int64_t es = g.dtype == QF_F32 ? 4 : 2;
+    qf::SampleDev a{};
+    a.logits = static_cast<const char*>(g.logits);
+    a.row_stride = g.logits_row_stride;
+    a.vocab = g.vocab;
+    a.slice = (int)(qf::ceil_div(qf::ceil_div(g.vocab, qf::kClusterCtas), 8) * 8);
+    a.vec = qf::aligned16(g.logits) && (g.logits_row_stride * es) % 16 == 0;
+    a.temperature = g.temperature;
+    a.top_k = g.top_k;
+    a.top_k_i64 = g.top_k_type == QF_I64;
+    a.top_p = g.top_p;
+    a.uniforms = g.uniforms;
+    a.seeds = g.seeds;
+    a.steps = g.steps;
+    a.out = g.out;
+    switch (g.dtype) {
+    case QF_F32: return qf::launch_sample<float>(a, g.batch, stream);
+    case QF_F16: return qf::launch_sample<__half>(a, g.batch, stream);
+    default: return qf::launch_sample<__nv_bfloat16>(a, g.batch, stream);
+    }
+}
+
+extern "C" int qf_uniforms_from_seeds(const int64_t* seeds, const int64_t* steps, int64_t n,
+                                      float* out, cudaStream_t stream) {
+    if (n < 0) return QF_ERR_INVALID;
+    if (n == 0) return QF_OK;
+    if (!seeds || !steps || !out) return QF_ERR_INVALID;
+    const int threads = 256;
+    qf::uniforms_kernel<<<(unsigned)qf::ceil_div(n, threads), threads, 0, stream>>>(seeds, steps,
+                                                                                    n, out);
+    return qf::check_launch();
+}
