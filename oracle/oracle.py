@@ -380,8 +380,15 @@ def sample_margins(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch
     rank - top_p| and the distance of u * total from the CDF values either
     side of the pick, all as fractions of the kept mass.  A row whose margin
     is below the float32 rounding of the reference's own softmax and cumsums
-    can legitimately land on either neighbour.  Returns (tokens, margins);
-    greedy rows get margin inf."""
+    can legitimately land on either neighbour.  Returns (tokens, margins,
+    slack); greedy rows get margin inf.
+
+    ``slack`` is, per row, how far the reference's own float32 arithmetic
+    moves its decisions: |sum of its float32 softmax over the kept ranks - 1|
+    (the reference never renormalises, so at top_p = 1.0 its top-p step drops
+    the tail whose exclusive cumsum passes 1.0, and every threshold scales by
+    that sum) plus 1e-6 for the float32 rounding of the cumsums.  Where a
+    row's margin exceeds its slack the reference's token is the exact one."""
     import numpy as np
 
     logits, temperature, top_k, top_p, uniforms = (
@@ -390,6 +397,7 @@ def sample_margins(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch
     s32 = (logits.float() / temperature.float().clamp(min=1e-5)[:, None]).numpy()
     toks = np.zeros(B, dtype=np.int64)
     margins = np.full(B, np.inf)
+    slack = np.full(B, 1e-6)
     for b in range(B):
         order = np.argsort(-s32[b].astype(np.float64), kind="stable")
         if float(temperature[b]) <= 0:
@@ -398,6 +406,8 @@ def sample_margins(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch
         k = int(top_k[b])
         k = k if 0 < k < V else V
         sv = s32[b][order[:k]].astype(np.float64)
+        p32 = torch.softmax(torch.from_numpy(s32[b][order[:k]]), dim=-1)
+        slack[b] += abs(float(p32.double().sum()) - 1.0)
         e = np.exp(sv - sv[0])
         p = e / e.sum()
         incl = np.cumsum(p)
@@ -419,4 +429,4 @@ def sample_margins(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch
         margin = min(margin, target - lo if r > 0 else np.inf, cdf[r] - target)
         toks[b] = order[r]
         margins[b] = margin
-    return torch.from_numpy(toks), torch.from_numpy(margins)
+    return torch.from_numpy(toks), torch.from_numpy(margins), torch.from_numpy(slack)

@@ -1,12 +1,19 @@
 """The batched sampler on the GPU against the reference's sample_tokens.
 
-Parity bar: the sampled token ids are integers and must be identical to the
-reference's, except on a row whose decision sits within 1e-6 (as a fraction
-of the kept probability mass) of a boundary -- the uniform's target against
-the CDF on either side of the pick, or the top-p threshold against the mass
-before the last kept / first dropped rank.  There the reference's own float32
-softmax and cumsums decide by their rounding, and either neighbour is a
-correct sample.  Such rows are found by oracle.sample_margins (float64).
+Parity bar.  Sampled token ids are integers, but the reference reaches them
+through float32 softmax and cumsums, and its token on a row moves with that
+rounding when the row's decision sits near a boundary.  The kernel does the
+same decisions in exact integer arithmetic on fixed-point masses, so:
+
+* against the float64 restatement of the algorithm (oracle.sample_margins):
+  identical tokens on every row whose margin exceeds 1e-7 of the kept mass
+  (the kernel's own precision: 2^-40 per element plus expf's last bit);
+* against the reference's tokens (the oracle's float32 torch restatement,
+  pinned to the reference's own outputs by tests/golden/sampling.pt):
+  identical on every row whose margin exceeds that row's float32 slack --
+  |sum of the reference's float32 softmax - 1| + 1e-6.  The reference never
+  renormalises, so at top_p = 1.0 it still drops the tail whose exclusive
+  cumsum passes 1.0, and every threshold moves with that sum.
 
 The behavioural tests restate the reference's own test file
 (tests/model/test_batch_sampling.py) against the CUDA path.
@@ -21,7 +28,7 @@ from tests.common import load_golden
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-EPS = 1e-6
+EXACT_EPS = 1e-7
 
 
 def _call(logit_rows, temperature, top_k, top_p, uniforms, dtype=torch.float32):
@@ -34,14 +41,20 @@ def _call(logit_rows, temperature, top_k, top_p, uniforms, dtype=torch.float32):
 
 
 def _check_against(out, expected, args, what):
-    """Identical tokens, except on rows within EPS of a decision boundary."""
+    """Exact tokens away from decision boundaries (see the module docstring);
+    returns how many rows differ from the reference in total."""
     out = out.cpu()
     assert out.dtype == torch.int64 and out.shape == expected.shape
-    _, margins = oracle.sample_margins(*args)
+    exact, margins, slack = oracle.sample_margins(*args)
+    bad = (out != exact) & (margins > EXACT_EPS)
+    assert not bad.any(), (f"{what}: rows {bad.nonzero().flatten().tolist()[:8]} differ from "
+                           f"exact arithmetic (got {out[bad][:8].tolist()}, "
+                           f"want {exact[bad][:8].tolist()})")
     differ = out != expected
-    bad = differ & (margins > EPS)
-    assert not bad.any(), (f"{what}: rows {bad.nonzero().flatten().tolist()[:8]} differ "
-                           f"(got {out[bad][:8].tolist()}, want {expected[bad][:8].tolist()})")
+    bad = differ & (margins > slack)
+    assert not bad.any(), (f"{what}: rows {bad.nonzero().flatten().tolist()[:8]} differ from "
+                           f"the reference (got {out[bad][:8].tolist()}, "
+                           f"want {expected[bad][:8].tolist()})")
     return int(differ.sum())
 
 

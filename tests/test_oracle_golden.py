@@ -242,13 +242,14 @@ def test_sampler_matches_reference():
 
 def test_sampler_float64_decisions_agree_away_from_boundaries():
     """The float64 restatement (used to tell which rows sit on a decision
-    boundary) picks the reference's token on every row whose margin is above
-    the float32 rounding of the reference's softmax and cumsums."""
+    boundary) picks the reference's token on every row whose margin exceeds
+    the reference's own float32 rounding (its softmax sum's distance from 1,
+    plus the cumsum rounding)."""
     g = load_golden("sampling.pt")
     for c in g["cases"]:
-        toks, margins = oracle.sample_margins(c["logits"], c["temperature"], c["top_k"],
-                                              c["top_p"], c["uniforms"])
-        clear = margins > 1e-6
+        toks, margins, slack = oracle.sample_margins(c["logits"], c["temperature"], c["top_k"],
+                                                     c["top_p"], c["uniforms"])
+        clear = margins > slack
         assert clear.float().mean() > 0.75, c["name"]
         assert toks[clear].tolist() == c["out"][clear].tolist(), c["name"]
 

@@ -50,9 +50,11 @@ constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kBins = 2048;                     // digits per level (level 3 uses 1024)
 constexpr int kOwn = kBins / kClusterCtas;      // combined bins each CTA holds
-constexpr int kPer = kOwn / 32;                 // of those, per lane of the scanning warp
+constexpr int kGroup = 32;                      // bins per group (one warp's scan)
+constexpr int kGroups = kBins / kGroup;         // 64: two per lane of the scanning warp
+constexpr int kOwnGroups = kOwn / kGroup;
 constexpr float kMassScale = 1099511627776.0f;  // 2^40
-static_assert(kOwn <= kThreads && kOwn % 32 == 0, "cluster size must be 4..64");
+static_assert(kOwn <= kThreads && kOwn % kGroup == 0 && kGroups == 64, "cluster size 4..64");
 using u64 = unsigned long long;
 
 struct SampleDev {
@@ -79,15 +81,35 @@ struct Crossing {
     u64 above_cnt, above_mas, cnt, mas;
 };
 
+// Candidates of one select: the elements under a digit prefix, at most
+// kCand of them across the cluster.
+constexpr int kCand = 512;
+
 struct SampleShared {
-    u64 mas[kBins];  // this CTA's histogram at the current level
-    uint32_t cnt[kBins];
-    u64 own1_mas[kOwn];  // level 1 summed over the cluster: this CTA's bin range
-    uint32_t own1_cnt[kOwn];
-    u64 own2_mas[kOwn];  // levels 2 and 3
-    uint32_t own2_cnt[kOwn];
-    u64 tot1_mas, tot2_mas;  // totals of the own ranges
-    uint32_t tot1_cnt, tot2_cnt;
+    union {
+        struct {  // this CTA's histogram at the current level; the mass is a
+                  // u64 kept as two u32 words (shared-memory u32 atomics are
+                  // native, u64 ones are not), the carry added explicitly
+            uint32_t cnt[kBins];
+            uint32_t mas_lo[kBins];
+            uint32_t mas_hi[kBins];
+        } h;
+        struct {  // candidate selects, two buffers used in turn
+            float s[2][kCand];      // this CTA's matching elements
+            uint32_t idx[2][kCand]; // and their vocabulary indices
+            u64 key[kCand];         // all of the cluster's: (order desc, index asc) as a u64
+            u64 w[kCand];           // and masses
+        } c;
+    } u;
+    // A level's histogram summed over the cluster: this CTA's range of bins,
+    // and every 32-bin group's totals (pushed here by the group's owner).
+    // lv[0]: level 1 (kept for every select of the row); lv[1]: levels 2, 3.
+    struct Level {
+        u64 own_mas[kOwn];
+        uint32_t own_cnt[kOwn];
+        u64 grp_mas[kGroups];
+        uint32_t grp_cnt[kGroups];
+    } lv[2];
     float max_s;  // this CTA's maximum and its lowest global index
     uint32_t max_idx;
     u64 red_mas[kWarps];
@@ -98,6 +120,13 @@ struct SampleShared {
     u64 z_all;
     int owner;
     uint32_t owner_j;
+    uint32_t cand_n[2];                     // this CTA's candidates, per buffer
+    uint32_t cand_pre[kClusterCtas + 1];    // the cluster's, prefix by rank
+    struct {
+        int found;
+        uint32_t idx;
+        u64 incl_cnt, incl_mas;
+    } cres;
 };
 
 __device__ __forceinline__ uint32_t order_key(float s) {
@@ -151,23 +180,34 @@ __device__ __forceinline__ void load_slice(const SampleDev& a, const T* row, int
                                            float* sv, float& best, uint32_t& best_i) {
     if (a.vec) {
         constexpr int PV = Dt<T>::kPerVec;
+        constexpr int U = 4;  // 16-byte loads in flight per thread
         const int nv = n / PV;
-        for (int c = threadIdx.x; c < nv; c += kThreads) {
-            const uint4 raw = ld_stream16(row + (int64_t)c * PV);
-            const T* x = reinterpret_cast<const T*>(&raw);
-            float v[PV];
+        for (int c0 = threadIdx.x; c0 < nv; c0 += U * kThreads) {
+            uint4 raw[U];
 #pragma unroll
-            for (int j = 0; j < PV; ++j) {
-                v[j] = scaled<T>(x[j], tc);
-                if (v[j] > best || best_i == 0xffffffffu) {
-                    best = v[j];
-                    best_i = (uint32_t)(c * PV + j);
-                }
+            for (int u = 0; u < U; ++u) {
+                const int c = c0 + u * kThreads;
+                if (c < nv) raw[u] = ld_stream16(row + (int64_t)c * PV);
             }
 #pragma unroll
-            for (int j = 0; j < PV; j += 4)
-                *reinterpret_cast<float4*>(sv + c * PV + j) = make_float4(v[j], v[j + 1], v[j + 2],
-                                                                          v[j + 3]);
+            for (int u = 0; u < U; ++u) {
+                const int c = c0 + u * kThreads;
+                if (c >= nv) break;
+                const T* x = reinterpret_cast<const T*>(&raw[u]);
+                float v[PV];
+#pragma unroll
+                for (int j = 0; j < PV; ++j) {
+                    v[j] = scaled<T>(x[j], tc);
+                    if (v[j] > best || best_i == 0xffffffffu) {
+                        best = v[j];
+                        best_i = (uint32_t)(c * PV + j);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < PV; j += 4)
+                    *reinterpret_cast<float4*>(sv + c * PV + j) =
+                        make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            }
         }
         for (int i = nv * PV + (int)threadIdx.x; i < n; i += kThreads) {
             const float v = scaled<T>(row[i], tc);
@@ -191,8 +231,9 @@ __device__ __forceinline__ void load_slice(const SampleDev& a, const T* row, int
 
 __device__ __forceinline__ void zero_hist(SampleShared& sm) {
     for (int i = threadIdx.x; i < kBins; i += kThreads) {
-        sm.cnt[i] = 0;
-        sm.mas[i] = 0;
+        sm.u.h.cnt[i] = 0;
+        sm.u.h.mas_lo[i] = 0;
+        sm.u.h.mas_hi[i] = 0;
     }
 }
 
@@ -204,60 +245,54 @@ __device__ __forceinline__ void build_hist(SampleShared& sm, const float* sv, in
         const uint32_t k = order_key(s);
         if (hi == 32 || (k >> hi) == prefix) {
             const uint32_t d = (k >> shift) & mask;
-            atomicAdd(&sm.cnt[d], 1u);
-            const u64 w = mass_of(s, m);
-            if (w) atomicAdd(&sm.mas[d], w);
+            atomicAdd(&sm.u.h.cnt[d], 1u);
+            const u64 w = mass_of(s, m);  // < 2^41
+            const uint32_t wl = (uint32_t)w, wh = (uint32_t)(w >> 32);
+            if (wl) {
+                const uint32_t old = atomicAdd(&sm.u.h.mas_lo[d], wl);
+                if (old + wl < old) atomicAdd(&sm.u.h.mas_hi[d], 1u);  // carry
+            }
+            if (wh) atomicAdd(&sm.u.h.mas_hi[d], wh);
         }
     });
 }
 
-// Sum the cluster's histograms over this CTA's bin range into own_* and its
-// total into tot_*.  Call between two cluster barriers.
-__device__ void combine(const cg::cluster_group& cl, SampleShared& sm, u64* own_mas,
-                        uint32_t* own_cnt, u64* tot_mas, uint32_t* tot_cnt) {
+// Sum the cluster's histograms over this CTA's bin range into lv[level], and
+// push each 32-bin group's totals into every CTA's lv[level].  Call between
+// two cluster barriers.
+__device__ void combine(const cg::cluster_group& cl, SampleShared& sm, int level) {
     const int rank = (int)cl.block_rank();
-    u64 m = 0;
-    uint32_t c = 0;
     if (threadIdx.x < kOwn) {
         const int b = rank * kOwn + threadIdx.x;
+        u64 m = 0;
+        uint32_t c = 0;
 #pragma unroll
         for (int q = 0; q < kClusterCtas; ++q) {
             const SampleShared* r = cl.map_shared_rank(&sm, q);
-            m += r->mas[b];
-            c += r->cnt[b];
+            m += ((u64)r->u.h.mas_hi[b] << 32) | r->u.h.mas_lo[b];
+            c += r->u.h.cnt[b];
         }
-        own_mas[threadIdx.x] = m;
-        own_cnt[threadIdx.x] = c;
-    }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (warp < kOwn / 32) {
+        sm.lv[level].own_mas[threadIdx.x] = m;
+        sm.lv[level].own_cnt[threadIdx.x] = c;
 #pragma unroll
         for (int o = 16; o; o >>= 1) {
-            m += __shfl_down_sync(0xffffffffu, m, o);
-            c += __shfl_down_sync(0xffffffffu, c, o);
+            m += __shfl_xor_sync(0xffffffffu, m, o);
+            c += __shfl_xor_sync(0xffffffffu, c, o);
         }
-        if (lane == 0) {
-            sm.red_mas[warp] = m;
-            sm.red_cnt[warp] = c;
+        const int lane = threadIdx.x & 31;
+        const int g = rank * kOwnGroups + (threadIdx.x >> 5);
+        if (lane < kClusterCtas) {
+            SampleShared* r = cl.map_shared_rank(&sm, lane);
+            r->lv[level].grp_mas[g] = m;
+            r->lv[level].grp_cnt[g] = c;
         }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        u64 tm = 0;
-        uint32_t tc = 0;
-        for (int w = 0; w < kOwn / 32; ++w) {
-            tm += sm.red_mas[w];
-            tc += sm.red_cnt[w];
-        }
-        *tot_mas = tm;
-        *tot_cnt = tc;
     }
 }
 
-__device__ __forceinline__ void scan_up(u64& c, u64& m, int lane) {
+__device__ __forceinline__ void scan_up(uint32_t& c, u64& m, int lane) {
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-        const u64 xc = __shfl_up_sync(0xffffffffu, c, o);
+        const uint32_t xc = __shfl_up_sync(0xffffffffu, c, o);
         const u64 xm = __shfl_up_sync(0xffffffffu, m, o);
         if (lane >= o) {
             c += xc;
@@ -268,81 +303,65 @@ __device__ __forceinline__ void scan_up(u64& c, u64& m, int lane) {
 
 // Warp 0: the first combined bin, in descending digit order, that is not empty
 // and whose inclusive cumulative weight (count or mass, starting from
-// above_*) reaches tau.  Every lane returns the same result.
-__device__ Crossing search(const cg::cluster_group& cl, SampleShared& sm, bool level1,
+// above_*) reaches tau.  The group totals are local; the 32 bins of the
+// chosen group are read from the CTA that owns them.  Every lane returns the
+// same result.
+__device__ Crossing search(const cg::cluster_group& cl, SampleShared& sm, int level,
                            bool by_mass, u64 tau, u64 above_cnt, u64 above_mas) {
     const int lane = threadIdx.x & 31;
+    const SampleShared::Level& L = sm.lv[level];
     Crossing f{};
-    // the CTAs' ranges, highest digits (last CTA) first
-    u64 tc = 0, tm = 0;
-    if (lane < kClusterCtas) {
-        const SampleShared* r = cl.map_shared_rank(&sm, kClusterCtas - 1 - lane);
-        tc = level1 ? r->tot1_cnt : r->tot2_cnt;
-        tm = level1 ? r->tot1_mas : r->tot2_mas;
-    }
-    u64 ic = tc, im = tm;
+    // groups, highest digits first: lane l takes groups 63 - 2l and 62 - 2l
+    const int ga = kGroups - 1 - 2 * lane, gb = ga - 1;
+    const uint32_t ca = L.grp_cnt[ga], cb = L.grp_cnt[gb];
+    const u64 ma = L.grp_mas[ga], mb = L.grp_mas[gb];
+    uint32_t ic = ca + cb;
+    u64 im = ma + mb;
     scan_up(ic, im, lane);
-    bool cond = lane < kClusterCtas && tc > 0 && (by_mass ? above_mas + im : above_cnt + ic) >= tau;
+    const uint32_t lc = ca + cb;
+    bool cond = lc > 0 && (by_mass ? above_mas + im : above_cnt + ic) >= tau;
     unsigned bal = __ballot_sync(0xffffffffu, cond);
     if (!bal) return f;
-    int L = __ffs(bal) - 1;
-    above_cnt += __shfl_sync(0xffffffffu, ic - tc, L);
-    above_mas += __shfl_sync(0xffffffffu, im - tm, L);
-    const int rho = kClusterCtas - 1 - L;
-    // that CTA's bins, descending; lane l takes kPer consecutive ones
-    const SampleShared* r = cl.map_shared_rank(&sm, rho);
-    const uint32_t* oc = level1 ? r->own1_cnt : r->own2_cnt;
-    const u64* om = level1 ? r->own1_mas : r->own2_mas;
-    uint32_t bc[kPer];
-    u64 bm[kPer];
-    u64 lc = 0, lm = 0;
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-        const int b = kOwn - 1 - (lane * kPer + i);
-        bc[i] = oc[b];
-        bm[i] = om[b];
-        lc += bc[i];
-        lm += bm[i];
+    int W = __ffs(bal) - 1;
+    u64 ec = above_cnt + ic - lc, em = above_mas + im - (ma + mb);
+    int g = ga;
+    if (!(ca > 0 && (by_mass ? em + ma : ec + ca) >= tau)) {
+        g = gb;
+        ec += ca;
+        em += ma;
     }
-    ic = lc;
-    im = lm;
+    g = __shfl_sync(0xffffffffu, g, W);
+    above_cnt = __shfl_sync(0xffffffffu, ec, W);
+    above_mas = __shfl_sync(0xffffffffu, em, W);
+    // that group's bins, highest first: lane l takes bin 31 - l
+    const int rho = g / kOwnGroups;
+    const int b = (g % kOwnGroups) * kGroup + kGroup - 1 - lane;
+    const SampleShared::Level& R = cl.map_shared_rank(&sm, rho)->lv[level];
+    const uint32_t bc = R.own_cnt[b];
+    const u64 bm = R.own_mas[b];
+    ic = bc;
+    im = bm;
     scan_up(ic, im, lane);
-    cond = lc > 0 && (by_mass ? above_mas + im : above_cnt + ic) >= tau;
+    cond = bc > 0 && (by_mass ? above_mas + im : above_cnt + ic) >= tau;
     bal = __ballot_sync(0xffffffffu, cond);
-    if (!bal) return f;  // unreachable: the range total crossed
-    L = __ffs(bal) - 1;
-    if (lane == L) {
-        u64 c0 = above_cnt + ic - lc, m0 = above_mas + im - lm;
-#pragma unroll
-        for (int i = 0; i < kPer; ++i) {
-            if (!f.found && bc[i] > 0 && (by_mass ? m0 + bm[i] : c0 + bc[i]) >= tau) {
-                f.found = 1;
-                f.digit = rho * kOwn + kOwn - 1 - (lane * kPer + i);
-                f.above_cnt = c0;
-                f.above_mas = m0;
-                f.cnt = bc[i];
-                f.mas = bm[i];
-            }
-            c0 += bc[i];
-            m0 += bm[i];
-        }
-    }
-    f.found = __shfl_sync(0xffffffffu, f.found, L);
-    f.digit = __shfl_sync(0xffffffffu, f.digit, L);
-    f.above_cnt = __shfl_sync(0xffffffffu, f.above_cnt, L);
-    f.above_mas = __shfl_sync(0xffffffffu, f.above_mas, L);
-    f.cnt = __shfl_sync(0xffffffffu, f.cnt, L);
-    f.mas = __shfl_sync(0xffffffffu, f.mas, L);
+    if (!bal) return f;  // unreachable: the group total crossed
+    W = __ffs(bal) - 1;
+    f.found = 1;
+    f.digit = rho * kOwn + __shfl_sync(0xffffffffu, b, W);
+    f.above_cnt = above_cnt + __shfl_sync(0xffffffffu, ic - bc, W);
+    f.above_mas = above_mas + __shfl_sync(0xffffffffu, im - bm, W);
+    f.cnt = __shfl_sync(0xffffffffu, bc, W);
+    f.mas = __shfl_sync(0xffffffffu, bm, W);
     return f;
 }
 
 // Run `search` on warp 0 and hand the result to the whole CTA.
 __device__ __forceinline__ Crossing search_all(const cg::cluster_group& cl, SampleShared& sm,
-                                               bool level1, bool by_mass, u64 tau, u64 above_cnt,
+                                               int level, bool by_mass, u64 tau, u64 above_cnt,
                                                u64 above_mas) {
     __syncthreads();  // everyone has read the previous result
     if (threadIdx.x < 32) {
-        const Crossing f = search(cl, sm, level1, by_mass, tau, above_cnt, above_mas);
+        const Crossing f = search(cl, sm, level, by_mass, tau, above_cnt, above_mas);
         if (threadIdx.x == 0) sm.res = f;
     }
     __syncthreads();
@@ -354,34 +373,141 @@ __device__ __forceinline__ Crossing deeper(const cg::cluster_group& cl, SampleSh
                                            const float* sv, int n, float m, int hi,
                                            uint32_t prefix, int shift, uint32_t mask, bool by_mass,
                                            u64 tau, const Crossing& parent) {
+    cl.sync();  // no CTA still reads another's candidate buffers (they share the histogram)
     zero_hist(sm);
     __syncthreads();
     build_hist(sm, sv, n, m, hi, prefix, shift, mask);
     cl.sync();  // every CTA's histogram is complete
-    combine(cl, sm, sm.own2_mas, sm.own2_cnt, &sm.tot2_mas, &sm.tot2_cnt);
-    cl.sync();  // every CTA's combined range is complete
-    return search_all(cl, sm, false, by_mass, tau, parent.above_cnt, parent.above_mas);
+    combine(cl, sm, 1);
+    cl.sync();  // every CTA's combined range and group totals are complete
+    return search_all(cl, sm, 1, by_mass, tau, parent.above_cnt, parent.above_mas);
 }
 
 // The rank where the cumulative weight first reaches tau.
 struct Selected {
     int found;
-    uint32_t key;       // order key of the rank's s
+    int has_idx;        // idx is the rank's vocabulary index
+    uint32_t idx;
+    uint32_t key;       // otherwise: the order key of the rank's s,
     uint32_t low_digit; // its level-3 digit (this CTA's cnt[] holds its local count)
-    u64 j;              // position inside the group of equal keys (index order)
+    u64 j;              // and its position inside the group of equal keys (index order)
     u64 incl_cnt;       // ranks up to and including it
     u64 incl_mas;       // their mass
 };
 
-__device__ Selected select_rank(const cg::cluster_group& cl, SampleShared& sm, const float* sv,
-                                int n, float m, bool by_mass, u64 tau) {
+// Select among the elements whose key has `prefix` above bit `hi` -- at most
+// kCand of them in the cluster -- the first (key desc, index asc) whose
+// cumulative weight, starting from above_*, reaches tau.  Every CTA gathers
+// all candidates over distributed shared memory and ranks each against the
+// others.  One cluster barrier; the candidate buffers alternate between
+// selects, so a CTA may fill the next buffer while others still read this one
+// (the buffer after that is only refilled once every CTA passed the next
+// select's barrier, i.e. finished reading).
+__device__ Selected select_candidates(const cg::cluster_group& cl, SampleShared& sm,
+                                      const float* sv, int n, int64_t base, float m, int hi,
+                                      uint32_t prefix, bool by_mass, u64 tau, u64 above_cnt,
+                                      u64 above_mas, int buf) {
+    if (threadIdx.x == 0) {
+        sm.cand_n[buf] = 0;
+        sm.cres.found = 0;
+    }
+    __syncthreads();
+    auto take = [&](float s, int i) {
+        if ((order_key(s) >> hi) == prefix) {
+            const uint32_t slot = atomicAdd(&sm.cand_n[buf], 1u);
+            if (slot < kCand) {
+                sm.u.c.s[buf][slot] = s;
+                sm.u.c.idx[buf][slot] = (uint32_t)(base + i);
+            }
+        }
+    };
+    const int n4 = n >> 2;
+    const float4* s4 = reinterpret_cast<const float4*>(sv);
+    for (int q = threadIdx.x; q < n4; q += kThreads) {
+        const float4 v = s4[q];
+        take(v.x, 4 * q);
+        take(v.y, 4 * q + 1);
+        take(v.z, 4 * q + 2);
+        take(v.w, 4 * q + 3);
+    }
+    for (int i = (n4 << 2) + (int)threadIdx.x; i < n; i += kThreads) take(sv[i], i);
+    cl.sync();  // every CTA's candidates are in place
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x < 32) {
+        uint32_t c = 0;
+        if (lane < kClusterCtas)
+            c = min(cl.map_shared_rank(&sm, lane)->cand_n[buf], (uint32_t)kCand);
+        uint32_t incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += x;
+        }
+        if (lane < kClusterCtas) sm.cand_pre[lane + 1] = incl;
+        if (lane == 0) sm.cand_pre[0] = 0;
+    }
+    __syncthreads();
+    const int total = (int)min(sm.cand_pre[kClusterCtas], (uint32_t)kCand);
+    const int t = threadIdx.x;
+    u64 key = 0, w = 0;
+    uint32_t idx = 0;
+    if (t < total) {
+        int q = 0;
+        while (q + 1 < kClusterCtas && (int)sm.cand_pre[q + 1] <= t) ++q;
+        const SampleShared* r = cl.map_shared_rank(&sm, q);
+        const float s = r->u.c.s[buf][t - sm.cand_pre[q]];
+        idx = r->u.c.idx[buf][t - sm.cand_pre[q]];
+        key = ((u64)(~order_key(s)) << 32) | idx;
+        w = mass_of(s, m);
+        sm.u.c.key[t] = key;
+        sm.u.c.w[t] = w;
+    }
+    __syncthreads();
+    if (t < total) {
+        uint32_t bc = 0;
+        u64 bm = 0;
+        for (int v = 0; v < total; ++v) {
+            const u64 kv = sm.u.c.key[v];
+            if (kv < key) {
+                ++bc;
+                bm += sm.u.c.w[v];
+            }
+        }
+        const u64 ec = above_cnt + bc, em = above_mas + bm;
+        const bool hit = by_mass ? (em + w >= tau && (em < tau || (tau == 0 && bc == 0)))
+                                 : ec + 1 == tau;
+        if (hit) {
+            sm.cres.found = 1;
+            sm.cres.idx = idx;
+            sm.cres.incl_cnt = ec + 1;
+            sm.cres.incl_mas = em + w;
+        }
+    }
+    __syncthreads();
     Selected out{};
-    const Crossing f1 = search_all(cl, sm, true, by_mass, tau, 0, 0);
+    out.found = sm.cres.found;
+    out.has_idx = 1;
+    out.idx = sm.cres.idx;
+    out.incl_cnt = sm.cres.incl_cnt;
+    out.incl_mas = sm.cres.incl_mas;
+    return out;
+}
+
+__device__ Selected select_rank(const cg::cluster_group& cl, SampleShared& sm, const float* sv,
+                                int n, int64_t base, float m, bool by_mass, u64 tau, int& nsel) {
+    Selected out{};
+    const Crossing f1 = search_all(cl, sm, 0, by_mass, tau, 0, 0);
     if (!f1.found) return out;
     const uint32_t p1 = (uint32_t)f1.digit;
+    if (f1.cnt <= (u64)kCand)
+        return select_candidates(cl, sm, sv, n, base, m, 21, p1, by_mass, tau, f1.above_cnt,
+                                 f1.above_mas, nsel++ & 1);
     const Crossing f2 = deeper(cl, sm, sv, n, m, 21, p1, 10, 2047u, by_mass, tau, f1);
     if (!f2.found) return out;
     const uint32_t p2 = (p1 << 11) | (uint32_t)f2.digit;
+    if (f2.cnt <= (u64)kCand)
+        return select_candidates(cl, sm, sv, n, base, m, 10, p2, by_mass, tau, f2.above_cnt,
+                                 f2.above_mas, nsel++ & 1);
     const Crossing f3 = deeper(cl, sm, sv, n, m, 10, p2, 0, 1023u, by_mass, tau, f2);
     if (!f3.found) return out;
     out.found = 1;
@@ -509,14 +635,17 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleDev a) 
     // ---- level 1 over the whole row: counts and masses ---------------------
     build_hist(sm, sv, n, m, 32, 0, 21, 2047u);
     cl.sync();
-    combine(cl, sm, sm.own1_mas, sm.own1_cnt, &sm.tot1_mas, &sm.tot1_cnt);
+    combine(cl, sm, 0);
     cl.sync();
-    u64 z_all = 0;
-    if (threadIdx.x == 0)
-        for (int q = 0; q < kClusterCtas; ++q) z_all += cl.map_shared_rank(&sm, q)->tot1_mas;
-    if (threadIdx.x == 0) sm.z_all = z_all;
+    if (threadIdx.x < 32) {
+        u64 z = sm.lv[0].grp_mas[lane] + sm.lv[0].grp_mas[lane + 32];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+        if (lane == 0) sm.z_all = z;
+    }
     __syncthreads();
-    z_all = sm.z_all;
+    const u64 z_all = sm.z_all;
+    int nsel = 0;  // candidate selects so far (picks their buffer)
 
     // ---- top-k -------------------------------------------------------------
     const int64_t V = a.vocab;
@@ -525,7 +654,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleDev a) 
     const u64 k_eff = (k > 0 && k < V) ? (u64)k : (u64)V;
     u64 z_k = z_all;
     if (k_eff < (u64)V) {
-        const Selected c = select_rank(cl, sm, sv, n, m, false, k_eff);
+        const Selected c = select_rank(cl, sm, sv, n, base, m, false, k_eff, nsel);
         if (c.found) z_k = c.incl_mas;
     }
 
@@ -535,7 +664,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleDev a) 
     if (top_p < 1.0f) {
         const double theta = (double)top_p * (double)z_k;
         const u64 tau = theta < 0.0 ? 0 : (u64)floor(theta) + 1;
-        const Selected c = select_rank(cl, sm, sv, n, m, true, tau);
+        const Selected c = select_rank(cl, sm, sv, n, base, m, true, tau, nsel);
         if (c.found && c.incl_cnt < k_eff) z_r = c.incl_mas;
     }
 
@@ -544,12 +673,14 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleDev a) 
                                : uniform_from_hash((uint64_t)a.seeds[row], (uint64_t)a.steps[row]);
     u64 tau = (u64)ceil((double)u * (double)z_r);
     if (tau > z_r) tau = z_r;
-    const Selected pick = select_rank(cl, sm, sv, n, m, true, tau);
-    if (pick.found) {
+    const Selected pick = select_rank(cl, sm, sv, n, base, m, true, tau, nsel);
+    if (pick.found && pick.has_idx) {
+        if (rank == 0 && threadIdx.x == 0) a.out[row] = pick.idx;
+    } else if (pick.found) {
         // which CTA holds the pick: prefix over the CTAs' counts of the key
         if (threadIdx.x < 32) {
             uint32_t c = 0;
-            if (lane < kClusterCtas) c = cl.map_shared_rank(&sm, lane)->cnt[pick.low_digit];
+            if (lane < kClusterCtas) c = cl.map_shared_rank(&sm, lane)->u.h.cnt[pick.low_digit];
             uint32_t incl = c;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -559,8 +690,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleDev a) 
             const bool own = lane < kClusterCtas && pick.j >= incl - c && pick.j < incl;
             const unsigned bal = __ballot_sync(0xffffffffu, own);
             if (lane == 0) {
-                const int L = bal ? __ffs(bal) - 1 : -1;
-                sm.owner = L;
+                sm.owner = bal ? __ffs(bal) - 1 : -1;
                 sm.owner_j = 0;
             }
             __syncwarp();
