@@ -688,7 +688,7 @@ def run_sample(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    B, V = SAMPLE_ROWS, SAMPLE_VOCAB
+    B, V = args.sample_rows, SAMPLE_VOCAB
     sets = [_sample_inputs(B, V, 1000 * rank + i, dev) for i in range(3)]
 
     def once(i):
@@ -770,7 +770,8 @@ def run_sample(args, rank: int, world: int, local_rank: int) -> dict | None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: seeded bf16 logits N(0, 16), mixed per-row sampling settings",
-        "config": {"workload": f"c3 decode step sampling: {B} rows x {V} vocab, bf16 logits",
+        "config": {"workload": f"c3 decode step sampling: {B} rows x {V} vocab, bf16 logits"
+                               + ("" if B == SAMPLE_ROWS else " (a profiling case, not the benchmark)"),
                    "rows": B, "vocab": V, "l2": "3 rotating logits buffers (233 MB > L2)"},
         "roofline": {"bound": "hbm", "kernel": "sample_kernel", "achieved": round(gbs, 1),
                      "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
@@ -797,6 +798,8 @@ def main() -> None:
                     help="CPU-baseline timing budget (ours arm)")
     ap.add_argument("--cpu-total", type=float, default=90.0,
                     help="total CPU time budget of the --impl reference run")
+    ap.add_argument("--sample-rows", type=int, default=SAMPLE_ROWS,
+                    help="rows of --workload sample (small profiling cases only)")
     ap.add_argument("--workload", choices=["layer", "attn", "prefill", "sample"],
                     default="layer",
                     help="layer: the fused-layer step (the headline); attn: decode attention; "

@@ -466,9 +466,23 @@ __device__ Selected select_candidates(const cg::cluster_group& cl, SampleShared&
     if (t < total) {
         uint32_t bc = 0;
         u64 bm = 0;
-        for (int v = 0; v < total; ++v) {
-            const u64 kv = sm.u.c.key[v];
-            if (kv < key) {
+        int v = 0;
+        for (; v + 4 <= total; v += 4) {
+            u64 kv[4], wv[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                kv[j] = sm.u.c.key[v + j];
+                wv[j] = sm.u.c.w[v + j];
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (kv[j] < key) {
+                    ++bc;
+                    bm += wv[j];
+                }
+        }
+        for (; v < total; ++v) {
+            if (sm.u.c.key[v] < key) {
                 ++bc;
                 bm += sm.u.c.w[v];
             }
@@ -608,20 +622,27 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleDev a) 
         sm.max_idx = bi;
     }
     cl.sync();
-    if (threadIdx.x == 0) {
+    if (threadIdx.x < 32) {  // lane q reads CTA q's maximum
         float b = -INFINITY;
         uint32_t bi = 0xffffffffu;
-        for (int q = 0; q < kClusterCtas; ++q) {
-            const SampleShared* r = cl.map_shared_rank(&sm, q);
-            const float s2 = r->max_s;
-            const uint32_t i2 = r->max_idx;
+        if (lane < kClusterCtas) {
+            const SampleShared* r = cl.map_shared_rank(&sm, lane);
+            b = r->max_s;
+            bi = r->max_idx;
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float s2 = __shfl_xor_sync(0xffffffffu, b, o);
+            const uint32_t i2 = __shfl_xor_sync(0xffffffffu, bi, o);
             if (i2 != 0xffffffffu && (bi == 0xffffffffu || better(s2, i2, b, bi))) {
                 b = s2;
                 bi = i2;
             }
         }
-        sm.row_max = b;
-        sm.row_argmax = bi;
+        if (lane == 0) {
+            sm.row_max = b;
+            sm.row_argmax = bi;
+        }
     }
     __syncthreads();
     const float m = sm.row_max;
