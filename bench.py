@@ -161,6 +161,26 @@ class Step:
             ev[5].record()
         return {"normed_in": y1, "q": q_out, "normed_post": y2, "residual": h2, "act": act}
 
+    def runners(self, t: dict) -> dict:
+        """Each kernel of the step as its own call, on the step's inputs (for
+        timing the kernels one at a time)."""
+        tsb, s = self.tsb, self.s
+        x0 = tsb.embedding(t["input_ids"], t["embed_weight"])
+        _, h1 = tsb.fused_add_rms_norm(t["x_mlp"], x0, t["input_layernorm"], s.eps)
+        q, k, v = self.W.qkv_views(t["qkv"], s)
+        return {
+            "embedding": lambda: tsb.embedding(t["input_ids"], t["embed_weight"]),
+            "add_rmsnorm_in": lambda: tsb.fused_add_rms_norm(t["x_mlp"], x0,
+                                                             t["input_layernorm"], s.eps),
+            "qk_norm_rope_store": lambda: tsb.qk_norm_rope_store(
+                q, k, v, t["q_norm"], t["k_norm"], s.eps, None, None, t["k_cache"],
+                t["v_cache"], t["block_mapping"], t["slot_mapping"], positions=t["positions"],
+                inv_freq=t["inv_freq"], want_k_out=False),
+            "add_rmsnorm_post": lambda: tsb.fused_add_rms_norm(
+                t["attn_out"], h1, t["post_attention_layernorm"], s.eps),
+            "silu_and_mul": lambda: tsb.silu_and_mul(t["gate_up"]),
+        }
+
     def bytes_per_token(self) -> dict[str, int]:
         bpt = self.W.bytes_per_token(self.s)
         return {
@@ -305,6 +325,26 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         per_kernel_us[name] = 1e3 * sum(e[j].elapsed_time(e[j + 1]) for e in evs) / kb
     tsb.check_errors(dev)
 
+    # ---- each kernel alone: a 256 MB read between launches evicts L2, so every
+    # launch reads its inputs from HBM; its own writes may still sit in L2 when
+    # its stop event fires (the next kernel in a real step pays that write-back).
+    iso_us = {}
+    flush = torch.ones(64 * 2 ** 20, dtype=torch.float32, device=dev)
+    for name, fn in step.runners(t).items():
+        ts = []
+        for i in range(25):
+            flush.sum()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            if i >= 5:
+                ts.append(1e3 * e0.elapsed_time(e1))
+        iso_us[name] = statistics.median(ts)
+    del flush
+    tsb.check_errors(dev)
+
     # ---- end to end from pinned host buffers ----------------------------------
     e2e = None if args.no_e2e else measure_e2e(args, step, t, dev, world)
 
@@ -320,6 +360,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         gbs = bpt[name] * T / (us * 1e-6) / 1e9
         kernels[name] = {"us": round(us, 2), "bytes_per_token": bpt[name],
                          "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+    kernels_isolated = {}
+    for name in Step.KERNELS:
+        us = iso_us[name]
+        gbs = bpt[name] * T / (us * 1e-6) / 1e9
+        kernels_isolated[name] = {"us": round(us, 2), "gbs": round(gbs, 1),
+                                  "frac": round(gbs / peak, 4)}
     attributed_ms = sum(per_kernel_us.values()) / 1e3
     dom = max(Step.KERNELS, key=lambda n: per_kernel_us[n])
     dom_gbs = bpt[dom] * T / (per_kernel_us[dom] * 1e-6) / 1e9
@@ -354,6 +400,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "kernels_note": "per-kernel CUDA-event times from a second pass with an event between "
                         f"every two launches ({kb} steps, {attributed_ms:.4f} ms per step); "
                         "the headline is the pass without them",
+        "kernels_isolated": kernels_isolated,
+        "kernels_isolated_note": "each kernel alone on the step's inputs, median of 20 launches, "
+                                 "a 256 MB read between launches so its inputs come from HBM; "
+                                 "its own writes may end in L2 (in the step, the next kernel "
+                                 "pays that write-back)",
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(dom_gbs, 1),
                      "peak": peak, "unit": "GB/s", "frac": round(dom_gbs / peak, 4),
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
@@ -650,7 +701,7 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> dict | None:
         "data": "synthetic: seeded lengths and activations of config c2",
         "config": {"workload": f"c2 prefill attention: {len(lens)} sequences, {T} tokens, causal",
                    "tokens": T, "max_seqlen": L},
-        "roofline": {"bound": "tensor", "kernel": "varlen_attn_mma_kernel", "achieved": round(tf, 1),
+        "roofline": {"bound": "tensor", "kernel": "varlen_attn_tc_kernel", "achieved": round(tf, 1),
                      "peak": peak, "unit": "TFLOP/s", "frac": round(tf / peak, 4),
                      "peak_source": f"{kind} bf16_tflops (cuBLAS burst)", "flops_per_launch": flops,
                      "traffic": None},

@@ -47,7 +47,8 @@ enum {
     QF_FLAG_BAD_BLOCK = 1, /* block index < 0 or >= num_blocks */
     QF_FLAG_BAD_SLOT = 2,  /* slot index < 0 or >= block_size */
     QF_FLAG_BAD_TOKEN = 4, /* token id < 0 or >= vocab */
-    QF_FLAG_BAD_TABLE = 8  /* logical block beyond the block table's length */
+    QF_FLAG_BAD_TABLE = 8, /* logical block beyond the block table's length */
+    QF_FLAG_TIMEOUT = 16   /* a kernel gave up waiting on its own tensor-core work */
 };
 
 /* ---------------------------------------------------------------------- */
@@ -286,6 +287,9 @@ typedef struct {
     int causal;
     float scale;
     int dtype;
+    int32_t* status;  /* optional: QF_FLAG_TIMEOUT */
+    int64_t total_q, total_k;  /* rows of q and of k/v (the tensor-core path's
+                                  bulk copies stay inside them); 0 = unknown */
 } qf_varlen_attention_args;
 
 int qf_varlen_attention(const qf_varlen_attention_args* args, cudaStream_t stream);

@@ -25,11 +25,13 @@ QF_I32, QF_I64 = 0, 1
 QF_OK, QF_ERR_INVALID, QF_ERR_UNSUPPORTED, QF_ERR_LAUNCH, QF_ERR_DEVICE = 0, 1, 2, 3, 4
 QF_ERR_SCRATCH = 5
 QF_FLAG_BAD_BLOCK, QF_FLAG_BAD_SLOT, QF_FLAG_BAD_TOKEN, QF_FLAG_BAD_TABLE = 1, 2, 4, 8
+QF_FLAG_TIMEOUT = 16
 
 FLAG_NAMES = {QF_FLAG_BAD_BLOCK: "block index outside the cache",
               QF_FLAG_BAD_SLOT: "slot index outside the block",
               QF_FLAG_BAD_TOKEN: "token id outside the vocabulary",
-              QF_FLAG_BAD_TABLE: "position beyond the block table"}
+              QF_FLAG_BAD_TABLE: "position beyond the block table",
+              QF_FLAG_TIMEOUT: "a kernel timed out waiting on its tensor-core work"}
 
 
 class QkNormRopeArgs(ctypes.Structure):
@@ -88,6 +90,8 @@ class VarlenAttentionArgs(ctypes.Structure):
         ("causal", c_int),
         ("scale", c_float),
         ("dtype", c_int),
+        ("status", c_vp),
+        ("total_q", c_i64), ("total_k", c_i64),
     ]
 
 

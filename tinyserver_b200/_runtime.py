@@ -94,6 +94,8 @@ def check_errors(device: torch.device | int | None = None) -> None:
     flags = read_flags(device)
     if flags:
         names = [n for bit, n in _capi.FLAG_NAMES.items() if flags & bit]
+        if flags & _capi.QF_FLAG_TIMEOUT:
+            raise RuntimeError("tinyserver_b200: " + "; ".join(names))
         raise IndexError("tinyserver_b200: " + "; ".join(names))
 
 

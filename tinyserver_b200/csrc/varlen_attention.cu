@@ -20,22 +20,10 @@
 // query row.
 #include "qf_common.cuh"
 #include "qf_mma.cuh"
+#include "qf_varlen.cuh"
 
 namespace qf {
 namespace {
-
-struct VarlenDev {
-    const char* q;
-    const char* k;
-    const char* v;
-    char* out;
-    int64_t qt, qh, kt, kh, vt, vh, ot, oh;  // token / head strides, elements
-    const int32_t* cu_q;
-    const int32_t* cu_k;
-    int batch, Hq, Hkv;
-    int causal;
-    float scale;
-};
 
 template <int D>
 struct VarTile {
@@ -315,8 +303,19 @@ int launch_varlen(const VarlenDev& a, int max_q, cudaStream_t stream) {
     }
 }
 
+#ifndef QF_VARLEN_TC
+#define QF_VARLEN_TC 1  // head_dim 128, 16-bit: the tcgen05 kernel
+#endif
+
 template <typename T>
 int dispatch_varlen(const VarlenDev& a, int64_t D, int max_q, cudaStream_t stream) {
+    if constexpr (sizeof(T) == 2) {
+        if (QF_VARLEN_TC && D == 128) {
+            const int rc = launch_varlen_tc(a, std::is_same<T, __nv_bfloat16>::value ? 1 : 0,
+                                            max_q, stream);
+            if (rc != QF_ERR_UNSUPPORTED) return rc;  // else: the mma.sync kernel below
+        }
+    }
     switch (D) {
     case 64: return launch_varlen<T, 64>(a, max_q, stream);
     case 128: return launch_varlen<T, 128>(a, max_q, stream);
@@ -367,6 +366,9 @@ extern "C" int qf_varlen_attention(const qf_varlen_attention_args* p, cudaStream
     a.Hkv = (int)g.num_kv_heads;
     a.causal = g.causal ? 1 : 0;
     a.scale = g.scale;
+    a.status = g.status;
+    a.total_q = g.total_q;
+    a.total_k = g.total_k;
     const int max_q = (int)std::min<int64_t>(g.max_seqlen_q, 1 << 30);
     switch (g.dtype) {
     case QF_F32: return qf::dispatch_varlen<float>(a, g.head_dim, max_q, stream);

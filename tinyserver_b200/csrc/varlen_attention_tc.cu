@@ -1,0 +1,513 @@
+// Prefill varlen attention on the 5th-generation tensor cores (tcgen05, TMEM,
+// TMA), warp-specialised.
+//
+// Same contract as the mma.sync kernel in varlen_attention.cu -- the
+// reference's flash_attn_varlen_func (server/model/kernels/
+// varlen_attention.py:145-218): packed sequences, causal masking with query i
+// keeping key j when i >= j (indices within the sequence, :111-114), GQA by
+// h / (Hq / Hkv), fp32 softmax, probabilities rounded to the value dtype
+// before they meet V (:121) -- for head_dim 128 in bf16 / fp16.
+//
+// One CTA per (256 queries = two 128-row tiles, sequence, query head), ten
+// warps:
+//   warps 0-3   softmax of tile 0 (thread t owns query row t: tensor-memory
+//               lane t), warps 4-7 the same for tile 1;
+//   warp 8      issues the MMAs (one thread);
+//   warp 9      issues the TMA copies (one thread).
+// Per 128-key block j and tile t:
+//   S_t = Q_t K_j^T   tcgen05.mma, Q and K from shared memory, S in TMEM
+//   softmax           the tile's warps read S_t (tcgen05.ld), mask, update the
+//                     running max m and sum l, rescale their rows of O_t when
+//                     m grows, and write P_t (rounded to the value dtype) over
+//                     the first 64 columns of S_t (tcgen05.st)
+//   O_t += P_t V_j    tcgen05.mma with A = P_t from TMEM, B = V_j from smem
+// The MMA thread orders the tensor core's work as S_0,0 S_1,0 | PV_0,0 S_0,1
+// PV_1,0 S_1,1 | ... so the tensor core runs one tile's P V and next S while
+// the other tile's warps are in their softmax.  tcgen05 operations of one
+// thread execute in issue order, which is what lets S_t,j+1 reuse the columns
+// P_t,j was read from.  K and V tiles arrive by TMA (3-D tensor maps over
+// head_dim x heads x tokens, 128-byte swizzle) into a two-stage ring guarded
+// by full / empty mbarriers.  Every wait is bounded: one that runs out sets
+// QF_FLAG_TIMEOUT and the kernel finishes without its result.
+//
+// Operand layout in shared memory: a 128-row tile of 128 16-bit elements is
+// two 16 KB slabs of 64 elements (128 bytes) per row in the canonical
+// 128-byte swizzle (row r at r * 128, 16-byte chunk c at (c ^ r % 8) * 16),
+// which is what a TMA box of 64 x 1 x 128 with SWIZZLE_128B writes.  Q and K
+// are read K-major, V MN-major (rows = keys, the reduction dimension).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <type_traits>
+
+#include "qf_common.cuh"
+#include "qf_varlen.cuh"
+
+namespace qf {
+namespace {
+
+constexpr int kRows = 128;                // rows per tile, keys per block
+constexpr int kSlab = kRows * 128;        // 16 KB
+constexpr int kTile = 2 * kSlab;          // 32 KB: one 128 x 128 tile
+constexpr int kSmem = 6 * kTile + 1024;   // Q[2], K[2], V[2] + alignment slack
+constexpr int kThreads = 320;
+constexpr int kMmaWarp = 8, kTmaWarp = 9;
+constexpr uint32_t kTmemCols = 512;       // S_0 | S_1 | O_0 | O_1
+constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at the boost clock
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// kind::f16 instruction descriptor: fp32 accumulator, A and B both bf16 (or
+// both fp16), A K-major, B K-major or MN-major, M = N = 128.
+__device__ __forceinline__ uint32_t idesc(uint32_t ab_bf16, uint32_t b_mn_major) {
+    return (1u << 4) | (ab_bf16 << 7) | (ab_bf16 << 10) | (b_mn_major << 16) |
+           ((128u >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t id,
+                                       uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(id), "r"(acc)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t id,
+                                       uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+        "r"(a_tmem), "l"(b), "r"(id), "r"(acc)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// Bounded wait for the completion of phase `parity`; false when it ran out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    const long long t0 = clock64();
+    while (true) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if (clock64() - t0 > kWaitCycles) return false;
+    }
+}
+
+// TMA: box {64 elements, 1 head, 128 tokens} at (x, head, token) into `dst`.
+__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, int x, int head,
+                                         int token, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(head), "r"(token), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_tile(char* tile, const CUtensorMap* map, int head, int token,
+                                         uint64_t* bar) {
+    tma_load(tile, map, 0, head, token, bar);
+    tma_load(tile + kSlab, map, 64, head, token, bar);
+}
+
+#define QF_TMEM_REGS32(r)                                                                       \
+    "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),         \
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), \
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),           \
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),           \
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+#define QF_TMEM_IN32(r)                                                                          \
+    "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),      \
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),        \
+        "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),      \
+        "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),      \
+        "r"(r[29]), "r"(r[30]), "r"(r[31])
+
+// 32 consecutive columns of this thread's lane (warp w reads lanes 32 (w % 4)..).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+        "%28, %29, %30, %31}, [%32];"
+        : QF_TMEM_REGS32(r)
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, "
+        "%10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, "
+        "%27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        QF_TMEM_IN32(r)
+        : "memory");
+}
+
+// 2^x with one MUFU instruction (subnormal results flush to 0).
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+struct TcBars {
+    uint64_t q_full;
+    uint64_t k_full[2], v_full[2], kv_empty[2];
+    uint64_t s_full[2], p_full[2];
+    uint64_t o_final;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    varlen_attn_tc_kernel(const VarlenDev a, const __grid_constant__ CUtensorMap tq,
+                          const __grid_constant__ CUtensorMap tk,
+                          const __grid_constant__ CUtensorMap tv) {
+    using P = Packed<T>;
+    extern __shared__ __align__(1024) char dsm[];
+    __shared__ TcBars bars;
+    __shared__ uint32_t tmem_slot;
+    __shared__ int failed;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int b = blockIdx.y, hq = blockIdx.z;
+    const int ctile = (int)gridDim.x - 1 - (int)blockIdx.x;  // longest causal tiles first
+    const int q0 = __ldg(a.cu_q + b), q_len = __ldg(a.cu_q + b + 1) - q0;
+    const int m0 = ctile * 2 * kRows;
+    if (m0 >= q_len) return;  // the whole CTA leaves before any barrier
+    const int k0 = __ldg(a.cu_k + b), k_len = __ldg(a.cu_k + b + 1) - k0;
+    const int hk = hq / (a.Hq / a.Hkv);
+    // key blocks per tile (tile 1 may hold no rows)
+    int nb[2];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        const int r0 = m0 + t * kRows;
+        const int kend = r0 >= q_len ? 0 : a.causal ? min(k_len, r0 + kRows) : k_len;
+        nb[t] = (kend + kRows - 1) / kRows;
+    }
+    const int nblk = max(nb[0], nb[1]);
+
+    const uint32_t raw = smem_u32(dsm);
+    char* base = dsm + (((raw + 1023u) & ~1023u) - raw);
+    char* sQ[2] = {base, base + kTile};
+    char* sK[2] = {base + 2 * kTile, base + 3 * kTile};
+    char* sV[2] = {base + 4 * kTile, base + 5 * kTile};
+
+    if (tid == 0) {
+        mbar_init(&bars.q_full, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&bars.k_full[s], 1);
+            mbar_init(&bars.v_full[s], 1);
+            mbar_init(&bars.kv_empty[s], 1);
+            mbar_init(&bars.s_full[s], 1);
+            mbar_init(&bars.p_full[s], kRows);
+        }
+        mbar_init(&bars.o_final, 1);
+        failed = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+
+    if (warp == kTmaWarp) {
+        // ---- producer: Q once, then K / V blocks through the two-stage ring
+        if (lane == 0 && nblk > 0) {
+            const int ntile = nb[1] > 0 ? 2 : 1;
+            mbar_expect_tx(&bars.q_full, (uint32_t)(ntile * kTile));
+            for (int t = 0; t < ntile; ++t) tma_tile(sQ[t], &tq, hq, q0 + m0 + t * kRows, &bars.q_full);
+            bool ok = true;
+            for (int j = 0; j < nblk; ++j) {
+                const int s = j & 1;
+                if (j >= 2) ok &= mbar_wait(&bars.kv_empty[s], (uint32_t)(((j - 2) >> 1) & 1));
+                mbar_expect_tx(&bars.k_full[s], (uint32_t)kTile);
+                tma_tile(sK[s], &tk, hk, k0 + j * kRows, &bars.k_full[s]);
+                mbar_expect_tx(&bars.v_full[s], (uint32_t)kTile);
+                tma_tile(sV[s], &tv, hk, k0 + j * kRows, &bars.v_full[s]);
+            }
+            if (!ok) atomicOr(&failed, 1);
+        }
+    } else if (warp == kMmaWarp) {
+        // ---- MMA issue: S_0,0 S_1,0 | PV_0,j S_0,j+1 PV_1,j S_1,j+1 | ...
+        if (lane == 0 && nblk > 0) {
+            const uint32_t bf = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+            const uint32_t id_qk = idesc(bf, 0u), id_pv = idesc(bf, 1u);
+            auto issue_s = [&](int t, int st) {
+                const uint32_t d = tmem + (uint32_t)(t * kRows);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {  // head_dim in steps of 16
+                    const uint32_t off = (uint32_t)((k >> 2) * kSlab + (k & 3) * 32);
+                    mma_ss(d, sdesc(smem_u32(sQ[t]) + off, 16, 1024),
+                           sdesc(smem_u32(sK[st]) + off, 16, 1024), id_qk, k > 0 ? 1u : 0u);
+                }
+                mma_commit(&bars.s_full[t]);
+            };
+            bool ok = mbar_wait(&bars.q_full, 0u);
+            ok &= mbar_wait(&bars.k_full[0], 0u);
+            tc_fence_after();
+            for (int t = 0; t < 2; ++t)
+                if (nb[t] > 0) issue_s(t, 0);
+            for (int j = 0; j < nblk; ++j) {
+                const int s = j & 1;
+                ok &= mbar_wait(&bars.v_full[s], (uint32_t)((j >> 1) & 1));
+                if (j + 1 < nblk) ok &= mbar_wait(&bars.k_full[s ^ 1], (uint32_t)(((j + 1) >> 1) & 1));
+                for (int t = 0; t < 2; ++t) {
+                    if (j >= nb[t]) continue;
+                    ok &= mbar_wait(&bars.p_full[t], (uint32_t)(j & 1));
+                    tc_fence_after();
+                    const uint32_t o = tmem + 256u + (uint32_t)(t * kRows);
+                    const uint32_t p = tmem + (uint32_t)(t * kRows);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)  // keys in steps of 16
+                        mma_ts(o, p + 8u * k, sdesc(smem_u32(sV[s]) + k * 2048, kSlab, 1024),
+                               id_pv, (j > 0 || k > 0) ? 1u : 0u);
+                    if (j + 1 < nb[t]) issue_s(t, s ^ 1);
+                }
+                mma_commit(&bars.kv_empty[s]);
+            }
+            mma_commit(&bars.o_final);
+            if (!ok) atomicOr(&failed, 1);
+        }
+    } else {
+        // ---- softmax of tile t, one query row per thread
+        const int t = warp >> 2;
+        const int r = tid & (kRows - 1);
+        const int qi = m0 + t * kRows + r;  // query row within the sequence
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        const uint32_t sS = tmem + lane_base + (uint32_t)(t * kRows);
+        const uint32_t sO = tmem + lane_base + 256u + (uint32_t)(t * kRows);
+        const float sl2 = a.scale * 1.4426950408889634f;  // scores in log2 units
+        float m = -INFINITY, l = 0.f;  // running max (log2 units) and sum
+        bool ok = true;
+        uint32_t sr[64];
+        for (int j = 0; j < nb[t]; ++j) {
+            ok &= mbar_wait(&bars.s_full[t], (uint32_t)(j & 1));
+            tc_fence_after();
+            const int kb = j * kRows;
+            // masking only on the blocks that reach past the sequence or the diagonal
+            const bool edge = kb + kRows > k_len || (a.causal && kb + kRows - 1 > m0 + t * kRows);
+            const int klim = a.causal ? min(k_len, qi + 1) : k_len;  // keys [kb, klim) count
+            // pass 1: row maximum of the raw scores
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                tmem_ld32(sS + 32 * c, sr);
+                tmem_wait_ld();
+                if (edge) {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        if (kb + 32 * c + e < klim) mx = fmaxf(mx, __uint_as_float(sr[e]));
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sr[e]));
+                }
+            }
+            mx *= sl2;
+            // the reference max moves only when the row max grows by more than
+            // 2^8: until then p stays below 256 and O needs no rescaling; the
+            // result O / l is the same either way
+            float corr = 1.f;
+            if (mx > m + 8.f) {
+                corr = m == -INFINITY ? 0.f : ex2(m - mx);
+                m = mx;
+            }
+            const bool grow = j > 0 && corr != 1.f;
+            if (__any_sync(0xffffffffu, grow)) {  // warp-wide access to this warp's rows of O_t
+                const float f = grow ? corr : 1.f;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t o[32];
+                    tmem_ld32(sO + 32 * c, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+                    tmem_st32(sO + 32 * c, o);
+                }
+            }
+            const float mref = m == -INFINITY ? 0.f : m;  // a row with no key yet: every p is 0
+            // pass 2: p = 2^(s * scale * log2e - m), rounded to the value dtype, in
+            // halves of 64 keys; half h's P goes over S columns [32h, 32h + 32),
+            // which half 0 has already read
+            float ps = 0.f;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                tmem_ld32(sS + 64 * h, sr);
+                tmem_ld32(sS + 64 * h + 32, sr + 32);
+                tmem_wait_ld();
+                uint32_t pk[32];
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const int c0 = 64 * h + 2 * e;
+                    float x0 = fmaf(__uint_as_float(sr[2 * e]), sl2, -mref);
+                    float x1 = fmaf(__uint_as_float(sr[2 * e + 1]), sl2, -mref);
+                    if (edge) {
+                        if (kb + c0 >= klim) x0 = -INFINITY;
+                        if (kb + c0 + 1 >= klim) x1 = -INFINITY;
+                    }
+                    const float p0 = ex2(x0), p1 = ex2(x1);
+                    ps += p0 + p1;
+                    pk[e] = P::pack(p0, p1);
+                }
+                tmem_st32(sS + 32 * h, pk);
+            }
+            l = l * corr + ps;
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&bars.p_full[t]);
+        }
+        if (nb[t] > 0) {
+            ok &= mbar_wait(&bars.o_final, 0u);
+            tc_fence_after();
+            constexpr int64_t ES = sizeof(T);
+            T* out = reinterpret_cast<T*>(a.out + ((int64_t)(q0 + qi) * a.ot + (int64_t)hq * a.oh) * ES);
+            const float inv = 1.f / l;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                tmem_ld32(sO + 64 * h, sr);
+                tmem_ld32(sO + 64 * h + 32, sr + 32);
+                tmem_wait_ld();
+                if (qi < q_len && ok) {
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        uint4 v;
+                        v.x = P::pack(__uint_as_float(sr[8 * c]) * inv, __uint_as_float(sr[8 * c + 1]) * inv);
+                        v.y = P::pack(__uint_as_float(sr[8 * c + 2]) * inv, __uint_as_float(sr[8 * c + 3]) * inv);
+                        v.z = P::pack(__uint_as_float(sr[8 * c + 4]) * inv, __uint_as_float(sr[8 * c + 5]) * inv);
+                        v.w = P::pack(__uint_as_float(sr[8 * c + 6]) * inv, __uint_as_float(sr[8 * c + 7]) * inv);
+                        *reinterpret_cast<uint4*>(out + 64 * h + 8 * c) = v;
+                    }
+                }
+            }
+        } else if (qi < q_len) {  // no keys: 0 / 0, as the reference's acc / l
+            constexpr int64_t ES = sizeof(T);
+            T* out = reinterpret_cast<T*>(a.out + ((int64_t)(q0 + qi) * a.ot + (int64_t)hq * a.oh) * ES);
+            for (int d = 0; d < 128; ++d) out[d] = Dt<T>::from_f(__int_as_float(0x7fc00000));
+        }
+        if (!ok) atomicOr(&failed, 1);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0 && failed) flag(a.status, QF_FLAG_TIMEOUT);
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
+// cuTensorMapEncodeTiled, looked up once through the runtime.
+PFN_cuTensorMapEncodeTiled encode_fn() {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled fn = nullptr;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(p);
+    });
+    return fn;
+}
+
+// A 3-D map over (head_dim = 128, heads, tokens) with 64 x 1 x 128 boxes.
+bool make_map(CUtensorMap* map, const char* ptr, int bf16, int64_t heads, int64_t tokens,
+              int64_t head_stride, int64_t token_stride) {
+    PFN_cuTensorMapEncodeTiled fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[3] = {128, (cuuint64_t)heads, (cuuint64_t)tokens};
+    const cuuint64_t strides[2] = {(cuuint64_t)head_stride * 2, (cuuint64_t)token_stride * 2};
+    const cuuint32_t box[3] = {64, 1, (cuuint32_t)kRows};
+    const cuuint32_t estride[3] = {1, 1, 1};
+    return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+              const_cast<char*>(ptr), dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename T>
+int launch_tc(const VarlenDev& a, int max_q, cudaStream_t stream) {
+    constexpr auto kernel = varlen_attn_tc_kernel<T>;
+    static std::atomic<bool> configured{false};
+    if (!configured.load(std::memory_order_relaxed)) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+        if (e != cudaSuccess) return launch_failed(e);
+        configured.store(true, std::memory_order_relaxed);
+    }
+    const int bf = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+    CUtensorMap tq, tk, tv;
+    if (!make_map(&tq, a.q, bf, a.Hq, a.total_q, a.qh, a.qt) ||
+        !make_map(&tk, a.k, bf, a.Hkv, a.total_k, a.kh, a.kt) ||
+        !make_map(&tv, a.v, bf, a.Hkv, a.total_k, a.vh, a.vt))
+        return QF_ERR_UNSUPPORTED;
+    const dim3 grid((unsigned)ceil_div(max_q, 2 * kRows), (unsigned)a.batch, (unsigned)a.Hq);
+    kernel<<<grid, kThreads, kSmem, stream>>>(a, tq, tk, tv);
+    return check_launch();
+}
+
+}  // namespace
+
+int launch_varlen_tc(const VarlenDev& a, int bf16, int max_q, cudaStream_t stream) {
+    if (a.total_q <= 0 || a.total_k <= 0 || a.total_q >= (1ll << 31) || a.total_k >= (1ll << 31))
+        return QF_ERR_UNSUPPORTED;
+    return bf16 ? launch_tc<__nv_bfloat16>(a, max_q, stream) : launch_tc<__half>(a, max_q, stream);
+}
+
+}  // namespace qf

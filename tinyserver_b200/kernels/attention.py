@@ -132,6 +132,9 @@ def flash_attn_varlen_func(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     a.causal = 1 if causal else 0
     a.scale = float(softmax_scale) if softmax_scale is not None else 1.0 / math.sqrt(D)
     a.dtype = tag
+    a.status = status_word(dev).data_ptr()
+    a.total_q, a.total_k = Tq, Tk
     rc = _capi.lib().qf_varlen_attention(a, stream_ptr(dev))
     _capi.check(rc, "flash_attn_varlen_func")
+    after_op(dev)
     return out
