@@ -197,9 +197,22 @@ __device__ __forceinline__ void tmem_wait_st() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// S_t = Q_t K_s^T (head_dim in steps of 16), then commit to `bar`.
+__device__ __forceinline__ void issue_s(uint32_t tmem, uint32_t ubase, int t, int s, uint32_t id,
+                                        uint64_t* bar) {
+    const uint32_t q = ubase + (uint32_t)(t * kTile), k = ubase + (uint32_t)((2 + s) * kTile);
+    const uint32_t d = tmem + (uint32_t)(t * kRows);
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (uint32_t)((kk >> 2) * kSlab + (kk & 3) * 32);
+        mma_ss(d, sdesc(q + off, 16, 1024), sdesc(k + off, 16, 1024), id, kk > 0 ? 1u : 0u);
+    }
+    mma_commit(bar);
+}
+
 struct TcBars {
     uint64_t q_full;
-    uint64_t k_full[2], v_full[2], kv_empty[2];
+    uint64_t k_full[2], v_full[2], k_empty[2], v_empty[2];
     uint64_t s_full[2], p_full[2];
     uint64_t o_final;
 };
@@ -216,35 +229,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ int failed;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int b = blockIdx.y, hq = blockIdx.z;
-    const int ctile = (int)gridDim.x - 1 - (int)blockIdx.x;  // longest causal tiles first
+    // CTAs are dispatched in block order, x fastest: every (sequence, head) pair
+    // of the last query tile first, then the tile before it, ... -- for causal
+    // attention the longest work first
+    const int b = (int)blockIdx.x / a.Hq, hq = (int)blockIdx.x % a.Hq;
+    const int ctile = (int)gridDim.y - 1 - (int)blockIdx.y;
     const int q0 = __ldg(a.cu_q + b), q_len = __ldg(a.cu_q + b + 1) - q0;
     const int m0 = ctile * 2 * kRows;
     if (m0 >= q_len) return;  // the whole CTA leaves before any barrier
     const int k0 = __ldg(a.cu_k + b), k_len = __ldg(a.cu_k + b + 1) - k0;
     const int hk = hq / (a.Hq / a.Hkv);
     // key blocks per tile (tile 1 may hold no rows)
-    int nb[2];
+    int nbx[2];
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
         const int r0 = m0 + t * kRows;
         const int kend = r0 >= q_len ? 0 : a.causal ? min(k_len, r0 + kRows) : k_len;
-        nb[t] = (kend + kRows - 1) / kRows;
+        nbx[t] = (kend + kRows - 1) / kRows;
     }
-    const int nblk = max(nb[0], nb[1]);
+    const int nb0 = nbx[0], nb1 = nbx[1];
+    const int nblk = max(nb0, nb1);
 
+    // operand tiles at 1024-byte aligned offsets: Q_t at t, K_s at 2 + s, V_s at 4 + s
     const uint32_t raw = smem_u32(dsm);
     char* base = dsm + (((raw + 1023u) & ~1023u) - raw);
-    char* sQ[2] = {base, base + kTile};
-    char* sK[2] = {base + 2 * kTile, base + 3 * kTile};
-    char* sV[2] = {base + 4 * kTile, base + 5 * kTile};
+    const uint32_t ubase = smem_u32(base);
 
     if (tid == 0) {
         mbar_init(&bars.q_full, 1);
         for (int s = 0; s < 2; ++s) {
             mbar_init(&bars.k_full[s], 1);
             mbar_init(&bars.v_full[s], 1);
-            mbar_init(&bars.kv_empty[s], 1);
+            mbar_init(&bars.k_empty[s], 1);
+            mbar_init(&bars.v_empty[s], 1);
             mbar_init(&bars.s_full[s], 1);
             mbar_init(&bars.p_full[s], kRows);
         }
@@ -265,19 +282,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = tmem_slot;
 
     if (warp == kTmaWarp) {
-        // ---- producer: Q once, then K / V blocks through the two-stage ring
-        if (lane == 0 && nblk > 0) {
-            const int ntile = nb[1] > 0 ? 2 : 1;
-            mbar_expect_tx(&bars.q_full, (uint32_t)(ntile * kTile));
-            for (int t = 0; t < ntile; ++t) tma_tile(sQ[t], &tq, hq, q0 + m0 + t * kRows, &bars.q_full);
+        // ---- producers: lane 0 loads Q, then the K blocks; lane 1 the V blocks.
+        // A K stage is refilled once the S MMAs that read it are done, a V
+        // stage once the P V MMAs are (two rings, so K runs ahead of V).
+        if (lane < 2 && nblk > 0) {
             bool ok = true;
+            if (lane == 0) {
+                const int ntile = nb1 > 0 ? 2 : 1;
+                mbar_expect_tx(&bars.q_full, (uint32_t)(ntile * kTile));
+                for (int t = 0; t < ntile; ++t)
+                    tma_tile(base + t * kTile, &tq, hq, q0 + m0 + t * kRows, &bars.q_full);
+            }
             for (int j = 0; j < nblk; ++j) {
                 const int s = j & 1;
-                if (j >= 2) ok &= mbar_wait(&bars.kv_empty[s], (uint32_t)(((j - 2) >> 1) & 1));
-                mbar_expect_tx(&bars.k_full[s], (uint32_t)kTile);
-                tma_tile(sK[s], &tk, hk, k0 + j * kRows, &bars.k_full[s]);
-                mbar_expect_tx(&bars.v_full[s], (uint32_t)kTile);
-                tma_tile(sV[s], &tv, hk, k0 + j * kRows, &bars.v_full[s]);
+                uint64_t* empty = lane == 0 ? &bars.k_empty[s] : &bars.v_empty[s];
+                uint64_t* full = lane == 0 ? &bars.k_full[s] : &bars.v_full[s];
+                if (j >= 2) ok &= mbar_wait(empty, (uint32_t)(((j - 2) >> 1) & 1));
+                mbar_expect_tx(full, (uint32_t)kTile);
+                tma_tile(base + ((lane == 0 ? 2 : 4) + s) * kTile, lane == 0 ? &tk : &tv, hk,
+                         k0 + j * kRows, full);
             }
             if (!ok) atomicOr(&failed, 1);
         }
@@ -286,38 +309,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0 && nblk > 0) {
             const uint32_t bf = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
             const uint32_t id_qk = idesc(bf, 0u), id_pv = idesc(bf, 1u);
-            auto issue_s = [&](int t, int st) {
-                const uint32_t d = tmem + (uint32_t)(t * kRows);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {  // head_dim in steps of 16
-                    const uint32_t off = (uint32_t)((k >> 2) * kSlab + (k & 3) * 32);
-                    mma_ss(d, sdesc(smem_u32(sQ[t]) + off, 16, 1024),
-                           sdesc(smem_u32(sK[st]) + off, 16, 1024), id_qk, k > 0 ? 1u : 0u);
-                }
-                mma_commit(&bars.s_full[t]);
-            };
             bool ok = mbar_wait(&bars.q_full, 0u);
             ok &= mbar_wait(&bars.k_full[0], 0u);
             tc_fence_after();
-            for (int t = 0; t < 2; ++t)
-                if (nb[t] > 0) issue_s(t, 0);
+            issue_s(tmem, ubase, 0, 0, id_qk, &bars.s_full[0]);
+            if (nb1 > 0) issue_s(tmem, ubase, 1, 0, id_qk, &bars.s_full[1]);
+            mma_commit(&bars.k_empty[0]);  // K_0 is free once these are done
             for (int j = 0; j < nblk; ++j) {
                 const int s = j & 1;
                 ok &= mbar_wait(&bars.v_full[s], (uint32_t)((j >> 1) & 1));
                 if (j + 1 < nblk) ok &= mbar_wait(&bars.k_full[s ^ 1], (uint32_t)(((j + 1) >> 1) & 1));
+#pragma unroll
                 for (int t = 0; t < 2; ++t) {
-                    if (j >= nb[t]) continue;
+                    const int nbt = t ? nb1 : nb0;
+                    if (j >= nbt) continue;
                     ok &= mbar_wait(&bars.p_full[t], (uint32_t)(j & 1));
                     tc_fence_after();
                     const uint32_t o = tmem + 256u + (uint32_t)(t * kRows);
                     const uint32_t p = tmem + (uint32_t)(t * kRows);
+                    const uint32_t v = ubase + (uint32_t)((4 + s) * kTile);
 #pragma unroll
                     for (int k = 0; k < 8; ++k)  // keys in steps of 16
-                        mma_ts(o, p + 8u * k, sdesc(smem_u32(sV[s]) + k * 2048, kSlab, 1024),
-                               id_pv, (j > 0 || k > 0) ? 1u : 0u);
-                    if (j + 1 < nb[t]) issue_s(t, s ^ 1);
+                        mma_ts(o, p + 8u * k, sdesc(v + k * 2048, kSlab, 1024), id_pv,
+                               (j > 0 || k > 0) ? 1u : 0u);
+                    if (j + 1 < nbt) issue_s(tmem, ubase, t, s ^ 1, id_qk, &bars.s_full[t]);
                 }
-                mma_commit(&bars.kv_empty[s]);
+                mma_commit(&bars.v_empty[s]);                     // V_j read
+                if (j + 1 < nblk) mma_commit(&bars.k_empty[s ^ 1]);  // K_j+1 read
             }
             mma_commit(&bars.o_final);
             if (!ok) atomicOr(&failed, 1);
@@ -325,6 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ---- softmax of tile t, one query row per thread
         const int t = warp >> 2;
+        const int nbt = t ? nb1 : nb0;
         const int r = tid & (kRows - 1);
         const int qi = m0 + t * kRows + r;  // query row within the sequence
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
@@ -334,82 +353,122 @@ __global__ void __launch_bounds__(kThreads, 1)
         float m = -INFINITY, l = 0.f;  // running max (log2 units) and sum
         bool ok = true;
         uint32_t sr[64];
-        for (int j = 0; j < nb[t]; ++j) {
+        for (int j = 0; j < nbt; ++j) {
             ok &= mbar_wait(&bars.s_full[t], (uint32_t)(j & 1));
             tc_fence_after();
             const int kb = j * kRows;
             // masking only on the blocks that reach past the sequence or the diagonal
             const bool edge = kb + kRows > k_len || (a.causal && kb + kRows - 1 > m0 + t * kRows);
             const int klim = a.causal ? min(k_len, qi + 1) : k_len;  // keys [kb, klim) count
-            // pass 1: row maximum of the raw scores
-            float mx = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                tmem_ld32(sS + 32 * c, sr);
+            // One pass: p = 2^(x - m) against the current reference max m while
+            // tracking the block's own max; only when that max exceeds m + 8 (p
+            // would pass 256) is the block redone against the new max, which
+            // then moves O.  A row's first block finds its max first.
+            float corr = 1.f, ps = 0.f;
+            bool redo = m == -INFINITY;
+            if (!redo) {
+                // S is read in 32-column quarters, the next one in flight while this
+                // one computes; P is kept in registers and stored only when no redo
+                // is needed (a redo re-reads S, which P overwrites)
+                const float mref = m;
+                float mx = -INFINITY;
+                uint32_t pk[64];
+                tmem_ld32(sS, sr);
                 tmem_wait_ld();
-                if (edge) {
 #pragma unroll
-                    for (int e = 0; e < 32; ++e)
-                        if (kb + 32 * c + e < klim) mx = fmaxf(mx, __uint_as_float(sr[e]));
+                for (int q = 0; q < 4; ++q) {
+                    uint32_t nx[32];
+                    if (q < 3) tmem_ld32(sS + 32 * (q + 1), nx);
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const int c0 = 32 * q + 2 * e;
+                        float x0 = fmaf(__uint_as_float(sr[2 * e]), sl2, -mref);
+                        float x1 = fmaf(__uint_as_float(sr[2 * e + 1]), sl2, -mref);
+                        if (edge) {
+                            if (kb + c0 >= klim) x0 = -INFINITY;
+                            if (kb + c0 + 1 >= klim) x1 = -INFINITY;
+                        }
+                        mx = fmaxf(mx, fmaxf(x0, x1));
+                        // x > 8 only in a block that is redone (its P is discarded)
+                        const float p0 = ex2(x0), p1 = ex2(x1);
+                        ps += p0 + p1;
+                        pk[16 * q + e] = P::pack(p0, p1);
+                    }
+                    if (q < 3) {
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) sr[e] = nx[e];
+                    }
+                }
+                redo = mx > 8.f;
+                if (redo) {
+                    ps = 0.f;
                 } else {
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sr[e]));
+                    tmem_st32(sS, pk);
+                    tmem_st32(sS + 32, pk + 32);
                 }
             }
-            mx *= sl2;
-            // the reference max moves only when the row max grows by more than
-            // 2^8: until then p stays below 256 and O needs no rescaling; the
-            // result O / l is the same either way
-            float corr = 1.f;
-            if (mx > m + 8.f) {
-                corr = m == -INFINITY ? 0.f : ex2(m - mx);
-                m = mx;
-            }
-            const bool grow = j > 0 && corr != 1.f;
-            if (__any_sync(0xffffffffu, grow)) {  // warp-wide access to this warp's rows of O_t
-                const float f = grow ? corr : 1.f;
+            if (__any_sync(0xffffffffu, redo)) {  // the warp-wide path: max first, then p
+                float mx = -INFINITY;
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t o[32];
-                    tmem_ld32(sO + 32 * c, o);
+                for (int c = 0; c < 4; c += 2) {
+                    tmem_ld32(sS + 32 * c, sr);
+                    tmem_ld32(sS + 32 * c + 32, sr + 32);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-                    tmem_st32(sO + 32 * c, o);
+                    for (int e = 0; e < 64; ++e)
+                        if (!edge || kb + 32 * c + e < klim) mx = fmaxf(mx, __uint_as_float(sr[e]));
                 }
-            }
-            const float mref = m == -INFINITY ? 0.f : m;  // a row with no key yet: every p is 0
-            // pass 2: p = 2^(s * scale * log2e - m), rounded to the value dtype, in
-            // halves of 64 keys; half h's P goes over S columns [32h, 32h + 32),
-            // which half 0 has already read
-            float ps = 0.f;
+                mx *= sl2;
+                if (redo && mx > m + 8.f) {
+                    corr = m == -INFINITY ? 0.f : ex2(m - mx);
+                    m = mx;
+                }
+                const bool grow = j > 0 && corr != 1.f;
+                if (__any_sync(0xffffffffu, grow)) {  // this warp's rows of O_t
+                    const float f = grow ? corr : 1.f;
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                tmem_ld32(sS + 64 * h, sr);
-                tmem_ld32(sS + 64 * h + 32, sr + 32);
-                tmem_wait_ld();
-                uint32_t pk[32];
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t o[32];
+                        tmem_ld32(sO + 32 * c, o);
+                        tmem_wait_ld();
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const int c0 = 64 * h + 2 * e;
-                    float x0 = fmaf(__uint_as_float(sr[2 * e]), sl2, -mref);
-                    float x1 = fmaf(__uint_as_float(sr[2 * e + 1]), sl2, -mref);
-                    if (edge) {
-                        if (kb + c0 >= klim) x0 = -INFINITY;
-                        if (kb + c0 + 1 >= klim) x1 = -INFINITY;
+                        for (int e = 0; e < 32; ++e)
+                            o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+                        tmem_st32(sO + 32 * c, o);
                     }
-                    const float p0 = ex2(x0), p1 = ex2(x1);
-                    ps += p0 + p1;
-                    pk[e] = P::pack(p0, p1);
                 }
-                tmem_st32(sS + 32 * h, pk);
+                if (redo) {
+                    const float mref = m == -INFINITY ? 0.f : m;  // no key yet: every p is 0
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        tmem_ld32(sS + 64 * h, sr);
+                        tmem_ld32(sS + 64 * h + 32, sr + 32);
+                        tmem_wait_ld();
+                        uint32_t pk[32];
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            const int c0 = 64 * h + 2 * e;
+                            float x0 = fmaf(__uint_as_float(sr[2 * e]), sl2, -mref);
+                            float x1 = fmaf(__uint_as_float(sr[2 * e + 1]), sl2, -mref);
+                            if (edge) {
+                                if (kb + c0 >= klim) x0 = -INFINITY;
+                                if (kb + c0 + 1 >= klim) x1 = -INFINITY;
+                            }
+                            const float p0 = ex2(x0), p1 = ex2(x1);
+                            ps += p0 + p1;
+                            pk[e] = P::pack(p0, p1);
+                        }
+                        tmem_st32(sS + 32 * h, pk);
+                    }
+                }
             }
             l = l * corr + ps;
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&bars.p_full[t]);
         }
-        if (nb[t] > 0) {
+        if (nbt > 0) {
             ok &= mbar_wait(&bars.o_final, 0u);
             tc_fence_after();
             constexpr int64_t ES = sizeof(T);
@@ -497,7 +556,9 @@ int launch_tc(const VarlenDev& a, int max_q, cudaStream_t stream) {
         !make_map(&tk, a.k, bf, a.Hkv, a.total_k, a.kh, a.kt) ||
         !make_map(&tv, a.v, bf, a.Hkv, a.total_k, a.vh, a.vt))
         return QF_ERR_UNSUPPORTED;
-    const dim3 grid((unsigned)ceil_div(max_q, 2 * kRows), (unsigned)a.batch, (unsigned)a.Hq);
+    if ((int64_t)a.batch * a.Hq >= (int64_t)1 << 31 || ceil_div(max_q, 2 * kRows) > 65535)
+        return QF_ERR_UNSUPPORTED;
+    const dim3 grid((unsigned)(a.batch * a.Hq), (unsigned)ceil_div(max_q, 2 * kRows));
     kernel<<<grid, kThreads, kSmem, stream>>>(a, tq, tk, tv);
     return check_launch();
 }
