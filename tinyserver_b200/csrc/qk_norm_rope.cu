@@ -310,6 +310,9 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const QkDev a) {
 #ifndef QF_QK_STEPS
 #define QF_QK_STEPS 2  // warp steps (HPW head rows each) per work unit
 #endif
+#ifndef QF_QK_CONTIG
+#define QF_QK_CONTIG 1  // each warp takes a contiguous range of units (a token's in a row)
+#endif
 
 template <typename T, int D>
 struct Wide {
@@ -524,7 +527,15 @@ __global__ void __launch_bounds__(256, Wide<T, D>::C > 4 ? 2 : QF_QK_MIN_CTAS)
     const IT warp = ((IT)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const IT nwarp = ((IT)gridDim.x * blockDim.x) >> 5;
     int64_t staged = -1;  // token whose cos/sin rows csm[wib] holds
+#if QF_QK_CONTIG
+    // consecutive units belong to one token, so the cos/sin staging and the
+    // position load happen once per token and warp
+    const IT u_begin = (IT)((uint64_t)units * warp / nwarp);
+    const IT u_end = (IT)((uint64_t)units * (warp + 1) / nwarp);
+    for (IT unit = u_begin; unit < u_end; ++unit) {
+#else
     for (IT unit = warp; unit < units; unit += nwarp) {
+#endif
         const IT tu = unit / upt;
         const int64_t t = (int64_t)tu;
         const int s0 = (int)(unit - tu * upt) * U;
