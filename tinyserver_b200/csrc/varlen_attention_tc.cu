@@ -352,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float sl2 = a.scale * 1.4426950408889634f;  // scores in log2 units
         float m = -INFINITY, l = 0.f;  // running max (log2 units) and sum
         bool ok = true;
-        uint32_t sr[64];
+        uint32_t sr[64];  // 32 used in the loop, 64 in the epilogue
         for (int j = 0; j < nbt; ++j) {
             ok &= mbar_wait(&bars.s_full[t], (uint32_t)(j & 1));
             tc_fence_after();
@@ -360,107 +360,81 @@ __global__ void __launch_bounds__(kThreads, 1)
             // masking only on the blocks that reach past the sequence or the diagonal
             const bool edge = kb + kRows > k_len || (a.causal && kb + kRows - 1 > m0 + t * kRows);
             const int klim = a.causal ? min(k_len, qi + 1) : k_len;  // keys [kb, klim) count
-            // One pass: p = 2^(x - m) against the current reference max m while
-            // tracking the block's own max; only when that max exceeds m + 8 (p
-            // would pass 256) is the block redone against the new max, which
-            // then moves O.  A row's first block finds its max first.
-            float corr = 1.f, ps = 0.f;
-            bool redo = m == -INFINITY;
-            if (!redo) {
-                // S is read in 32-column quarters, the next one in flight while this
-                // one computes; P is kept in registers and stored only when no redo
-                // is needed (a redo re-reads S, which P overwrites)
-                const float mref = m;
-                float mx = -INFINITY;
-                uint32_t pk[64];
-                tmem_ld32(sS, sr);
-                tmem_wait_ld();
+            // pass 1: the block's row max, S read in 32-column quarters with the
+            // next quarter in flight
+            float mx = -INFINITY;
+            tmem_ld32(sS, sr);
+            tmem_wait_ld();
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    uint32_t nx[32];
-                    if (q < 3) tmem_ld32(sS + 32 * (q + 1), nx);
+            for (int q = 0; q < 4; ++q) {
+                uint32_t nx[32];
+                if (q < 3) tmem_ld32(sS + 32 * (q + 1), nx);
+                if (edge) {
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const int c0 = 32 * q + 2 * e;
-                        float x0 = fmaf(__uint_as_float(sr[2 * e]), sl2, -mref);
-                        float x1 = fmaf(__uint_as_float(sr[2 * e + 1]), sl2, -mref);
-                        if (edge) {
-                            if (kb + c0 >= klim) x0 = -INFINITY;
-                            if (kb + c0 + 1 >= klim) x1 = -INFINITY;
-                        }
-                        mx = fmaxf(mx, fmaxf(x0, x1));
-                        // x > 8 only in a block that is redone (its P is discarded)
-                        const float p0 = ex2(x0), p1 = ex2(x1);
-                        ps += p0 + p1;
-                        pk[16 * q + e] = P::pack(p0, p1);
-                    }
-                    if (q < 3) {
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) sr[e] = nx[e];
-                    }
-                }
-                redo = mx > 8.f;
-                if (redo) {
-                    ps = 0.f;
+                    for (int e = 0; e < 32; ++e)
+                        if (kb + 32 * q + e < klim) mx = fmaxf(mx, __uint_as_float(sr[e]));
                 } else {
-                    tmem_st32(sS, pk);
-                    tmem_st32(sS + 32, pk + 32);
-                }
-            }
-            if (__any_sync(0xffffffffu, redo)) {  // the warp-wide path: max first, then p
-                float mx = -INFINITY;
 #pragma unroll
-                for (int c = 0; c < 4; c += 2) {
-                    tmem_ld32(sS + 32 * c, sr);
-                    tmem_ld32(sS + 32 * c + 32, sr + 32);
+                    for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sr[e]));
+                }
+                if (q < 3) {
                     tmem_wait_ld();
 #pragma unroll
-                    for (int e = 0; e < 64; ++e)
-                        if (!edge || kb + 32 * c + e < klim) mx = fmaxf(mx, __uint_as_float(sr[e]));
+                    for (int e = 0; e < 32; ++e) sr[e] = nx[e];
                 }
-                mx *= sl2;
-                if (redo && mx > m + 8.f) {
-                    corr = m == -INFINITY ? 0.f : ex2(m - mx);
-                    m = mx;
+            }
+            mx *= sl2;
+            // the reference max moves only when the row max grows by more than
+            // 2^8: until then p stays below 256 and O needs no rescaling; the
+            // result O / l is the same either way
+            float corr = 1.f;
+            if (mx > m + 8.f) {
+                corr = m == -INFINITY ? 0.f : ex2(m - mx);
+                m = mx;
+            }
+            const bool grow = j > 0 && corr != 1.f;
+            if (__any_sync(0xffffffffu, grow)) {  // this warp's rows of O_t
+                const float f = grow ? corr : 1.f;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t o[32];
+                    tmem_ld32(sO + 32 * c, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+                    tmem_st32(sO + 32 * c, o);
                 }
-                const bool grow = j > 0 && corr != 1.f;
-                if (__any_sync(0xffffffffu, grow)) {  // this warp's rows of O_t
-                    const float f = grow ? corr : 1.f;
+            }
+            const float mref = m == -INFINITY ? 0.f : m;  // a row with no key yet: every p is 0
+            // pass 2: p = 2^(s * scale * log2e - m), rounded to the value dtype and
+            // packed in pairs, quarter by quarter; each 64 keys' P goes over S
+            // columns [32h, 32h + 32), already read
+            float ps = 0.f;
+            uint32_t pk[32];
+            tmem_ld32(sS, sr);
+            tmem_wait_ld();
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        uint32_t o[32];
-                        tmem_ld32(sO + 32 * c, o);
-                        tmem_wait_ld();
+            for (int q = 0; q < 4; ++q) {
+                uint32_t nx[32];
+                if (q < 3) tmem_ld32(sS + 32 * (q + 1), nx);
 #pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-                        tmem_st32(sO + 32 * c, o);
+                for (int e = 0; e < 16; ++e) {
+                    const int c0 = 32 * q + 2 * e;
+                    float x0 = fmaf(__uint_as_float(sr[2 * e]), sl2, -mref);
+                    float x1 = fmaf(__uint_as_float(sr[2 * e + 1]), sl2, -mref);
+                    if (edge) {
+                        if (kb + c0 >= klim) x0 = -INFINITY;
+                        if (kb + c0 + 1 >= klim) x1 = -INFINITY;
                     }
+                    const float p0 = ex2(x0), p1 = ex2(x1);
+                    ps += p0 + p1;
+                    pk[16 * (q & 1) + e] = P::pack(p0, p1);
                 }
-                if (redo) {
-                    const float mref = m == -INFINITY ? 0.f : m;  // no key yet: every p is 0
+                if (q & 1) tmem_st32(sS + 32 * (q >> 1), pk);
+                if (q < 3) {
+                    tmem_wait_ld();
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        tmem_ld32(sS + 64 * h, sr);
-                        tmem_ld32(sS + 64 * h + 32, sr + 32);
-                        tmem_wait_ld();
-                        uint32_t pk[32];
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) {
-                            const int c0 = 64 * h + 2 * e;
-                            float x0 = fmaf(__uint_as_float(sr[2 * e]), sl2, -mref);
-                            float x1 = fmaf(__uint_as_float(sr[2 * e + 1]), sl2, -mref);
-                            if (edge) {
-                                if (kb + c0 >= klim) x0 = -INFINITY;
-                                if (kb + c0 + 1 >= klim) x1 = -INFINITY;
-                            }
-                            const float p0 = ex2(x0), p1 = ex2(x1);
-                            ps += p0 + p1;
-                            pk[e] = P::pack(p0, p1);
-                        }
-                        tmem_st32(sS + 32 * h, pk);
-                    }
+                    for (int e = 0; e < 32; ++e) sr[e] = nx[e];
                 }
             }
             l = l * corr + ps;
