@@ -141,3 +141,17 @@ def test_fewer_keys_than_queries():
         tsb.check_errors()
         assert_close(out, expected, f"lq != lk causal={causal}", min_exact=0.0)
         _as_accurate_as_reference(out, q, k, v, cq, ck, causal, f"lq != lk causal={causal}")
+
+
+@pytest.mark.parametrize("scale", [0.25, -0.05, 0.0])
+def test_softmax_scale_any_sign(scale):
+    """An explicit softmax_scale, negative and zero included (the row max is
+    taken after scaling, as the reference's), at head_dim 128."""
+    lens = [5, 200, 300]
+    q, k, v, cu = _packed(lens, 8, 4, 128, torch.bfloat16, seed=int(scale * 100) + 50)
+    expected = oracle.varlen_attention(q, k, v, cu, cu, True, softmax_scale=scale)
+    out = tsb.flash_attn_varlen_func(q.to(DEV), k.to(DEV), v.to(DEV), cu.to(DEV), cu.to(DEV),
+                                     max(lens), max(lens), True, softmax_scale=scale)
+    tsb.check_errors()
+    assert torch.isfinite(out).all()
+    assert_close(out, expected, f"scale={scale}", min_exact=0.0)

@@ -183,11 +183,47 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
         : "memory");
 }
 
+// 16 consecutive columns of this thread's lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, "
+        "%10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+        "r"(r[15])
+        : "memory");
+}
+
 // 2^x with one MUFU instruction (subnormal results flush to 0).
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// max(a, b, c) in one instruction.
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// (d0, d1) = (a0 * b + c, a1 * b + c) as one packed fp32x2 FMA.
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\tmov.b64 rc, {%5, %5};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+
+// (s0, s1) += (a0, a1) as one packed fp32x2 add.
+__device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
+    asm("{\n\t.reg .b64 rs, ra;\n\t"
+        "mov.b64 rs, {%0, %1};\n\tmov.b64 ra, {%2, %3};\n\t"
+        "add.f32x2 rs, rs, ra;\n\tmov.b64 {%0, %1}, rs;\n\t}"
+        : "+f"(s0), "+f"(s1)
+        : "f"(a0), "f"(a1));
 }
 
 __device__ __forceinline__ void tmem_wait_ld() {
@@ -361,8 +397,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool edge = kb + kRows > k_len || (a.causal && kb + kRows - 1 > m0 + t * kRows);
             const int klim = a.causal ? min(k_len, qi + 1) : k_len;  // keys [kb, klim) count
             // pass 1: the block's row max, S read in 32-column quarters with the
-            // next quarter in flight
-            float mx = -INFINITY;
+            // next quarter in flight, four independent three-input max chains
+            // (sl2 > 0: the launcher sends other scales to the mma.sync kernel)
+            const int lim = klim - kb;  // columns [lim, 128) are masked
+            float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
             tmem_ld32(sS, sr);
             tmem_wait_ld();
 #pragma unroll
@@ -372,10 +410,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (edge) {
 #pragma unroll
                     for (int e = 0; e < 32; ++e)
-                        if (kb + 32 * q + e < klim) mx = fmaxf(mx, __uint_as_float(sr[e]));
-                } else {
+                        if (32 * q + e >= lim) sr[e] = __float_as_uint(-INFINITY);
+                }
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sr[e]));
+                for (int e = 0; e < 32; e += 8) {
+                    mx0 = max3(mx0, __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]));
+                    mx1 = max3(mx1, __uint_as_float(sr[e + 2]), __uint_as_float(sr[e + 3]));
+                    mx2 = max3(mx2, __uint_as_float(sr[e + 4]), __uint_as_float(sr[e + 5]));
+                    mx3 = max3(mx3, __uint_as_float(sr[e + 6]), __uint_as_float(sr[e + 7]));
                 }
                 if (q < 3) {
                     tmem_wait_ld();
@@ -383,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int e = 0; e < 32; ++e) sr[e] = nx[e];
                 }
             }
-            mx *= sl2;
+            const float mx = max3(mx0, mx1, fmaxf(mx2, mx3)) * sl2;
             // the reference max moves only when the row max grows by more than
             // 2^8: until then p stays below 256 and O needs no rescaling; the
             // result O / l is the same either way
@@ -407,10 +449,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const float mref = m == -INFINITY ? 0.f : m;  // a row with no key yet: every p is 0
             // pass 2: p = 2^(s * scale * log2e - m), rounded to the value dtype and
-            // packed in pairs, quarter by quarter; each 64 keys' P goes over S
-            // columns [32h, 32h + 32), already read
-            float ps = 0.f;
-            uint32_t pk[32];
+            // packed in pairs, quarter by quarter; each quarter's P goes over S
+            // columns [16q, 16q + 16), already read; the row sum in two packed
+            // accumulator pairs
+            float ps0 = 0.f, ps1 = 0.f, ps2 = 0.f, ps3 = 0.f;
+            uint32_t pk[16];
             tmem_ld32(sS, sr);
             tmem_wait_ld();
 #pragma unroll
@@ -420,24 +463,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
                     const int c0 = 32 * q + 2 * e;
-                    float x0 = fmaf(__uint_as_float(sr[2 * e]), sl2, -mref);
-                    float x1 = fmaf(__uint_as_float(sr[2 * e + 1]), sl2, -mref);
+                    float x0, x1;
+                    fma2(x0, x1, __uint_as_float(sr[2 * e]), __uint_as_float(sr[2 * e + 1]), sl2,
+                         -mref);
                     if (edge) {
-                        if (kb + c0 >= klim) x0 = -INFINITY;
-                        if (kb + c0 + 1 >= klim) x1 = -INFINITY;
+                        if (c0 >= lim) x0 = -INFINITY;
+                        if (c0 + 1 >= lim) x1 = -INFINITY;
                     }
                     const float p0 = ex2(x0), p1 = ex2(x1);
-                    ps += p0 + p1;
-                    pk[16 * (q & 1) + e] = P::pack(p0, p1);
+                    if (e & 1)
+                        add2(ps2, ps3, p0, p1);
+                    else
+                        add2(ps0, ps1, p0, p1);
+                    pk[e] = P::pack(p0, p1);
                 }
-                if (q & 1) tmem_st32(sS + 32 * (q >> 1), pk);
+                // keys [32q, 32q + 32) -> columns [16q, 16q + 16): read already,
+                // and below the quarter in flight
+                tmem_st16(sS + 16 * q, pk);
                 if (q < 3) {
                     tmem_wait_ld();
 #pragma unroll
                     for (int e = 0; e < 32; ++e) sr[e] = nx[e];
                 }
             }
-            l = l * corr + ps;
+            l = l * corr + ((ps0 + ps1) + (ps2 + ps3));
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&bars.p_full[t]);
@@ -542,6 +591,7 @@ int launch_tc(const VarlenDev& a, int max_q, cudaStream_t stream) {
 int launch_varlen_tc(const VarlenDev& a, int bf16, int max_q, cudaStream_t stream) {
     if (a.total_q <= 0 || a.total_k <= 0 || a.total_q >= (1ll << 31) || a.total_k >= (1ll << 31))
         return QF_ERR_UNSUPPORTED;
+    if (!(a.scale > 0.f) || isinf(a.scale)) return QF_ERR_UNSUPPORTED;  // max(s) * scale is the max
     return bf16 ? launch_tc<__nv_bfloat16>(a, max_q, stream) : launch_tc<__half>(a, max_q, stream);
 }
 
