@@ -290,6 +290,13 @@ typedef struct {
     int32_t* status;  /* optional: QF_FLAG_TIMEOUT */
     int64_t total_q, total_k;  /* rows of q and of k/v (the tensor-core path's
                                   bulk copies stay inside them); 0 = unknown */
+    int32_t* work_counter;     /* optional, 2 words of device memory, zero
+                                  before their first use: the tensor-core path
+                                  then runs one CTA per SM, claiming work from
+                                  it, and leaves it at zero again when the call
+                                  completes.  Calls that may overlap on the GPU
+                                  (other streams) need counters of their own.
+                                  NULL: one CTA per 256-query tile pair. */
 } qf_varlen_attention_args;
 
 int qf_varlen_attention(const qf_varlen_attention_args* args, cudaStream_t stream);

@@ -155,3 +155,44 @@ def test_softmax_scale_any_sign(scale):
     tsb.check_errors()
     assert torch.isfinite(out).all()
     assert_close(out, expected, f"scale={scale}", min_exact=0.0)
+
+
+def _via_capi(q, k, v, cu, max_len, causal, counter):
+    """One call through the C ABI with or without a work counter."""
+    from tinyserver_b200 import _capi
+    from tinyserver_b200._runtime import status_word, stream_ptr
+
+    out = torch.empty_like(q)
+    a = _capi.VarlenAttentionArgs()
+    a.q, a.q_stride_token, a.q_stride_head = q.data_ptr(), q.stride(0), q.stride(1)
+    a.k, a.k_stride_token, a.k_stride_head = k.data_ptr(), k.stride(0), k.stride(1)
+    a.v, a.v_stride_token, a.v_stride_head = v.data_ptr(), v.stride(0), v.stride(1)
+    a.out, a.out_stride_token, a.out_stride_head = out.data_ptr(), out.stride(0), out.stride(1)
+    a.cu_seqlens_q = a.cu_seqlens_k = cu.data_ptr()
+    a.batch, a.max_seqlen_q = cu.numel() - 1, max_len
+    a.num_q_heads, a.num_kv_heads, a.head_dim = q.shape[1], k.shape[1], q.shape[2]
+    a.causal = int(causal)
+    a.scale = q.shape[2] ** -0.5
+    a.dtype = _capi.QF_BF16
+    a.status = status_word(q.device).data_ptr()
+    a.total_q, a.total_k = q.shape[0], k.shape[0]
+    a.work_counter = None if counter is None else counter.data_ptr()
+    _capi.check(_capi.lib().qf_varlen_attention(a, stream_ptr(q.device)), "varlen")
+    return out
+
+
+@pytest.mark.parametrize("lens", [[3000, 40, 900, 1], [130] * 3, [2048] * 40])
+def test_persistent_schedule_matches_one_cta_per_item(lens):
+    """Persistent CTAs claiming items from a counter compute each item exactly
+    as a CTA of its own would (bit-identical outputs), over fewer items than
+    SMs, and many more; the counter is back at zero after every call, so the
+    next call on the same counter sees all items again."""
+    q, k, v, cu = _packed(lens, 16, 8, 128, torch.bfloat16, seed=len(lens))
+    q, k, v, cu = q.to(DEV), k.to(DEV), v.to(DEV), cu.to(DEV)
+    one = _via_capi(q, k, v, cu, max(lens), True, None)
+    counter = torch.zeros(2, dtype=torch.int32, device=DEV)
+    for _ in range(3):
+        out = _via_capi(q, k, v, cu, max(lens), True, counter)
+        tsb.check_errors()
+        assert torch.equal(out, one)
+        assert counter.tolist() == [0, 0]

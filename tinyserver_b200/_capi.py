@@ -92,6 +92,7 @@ class VarlenAttentionArgs(ctypes.Structure):
         ("dtype", c_int),
         ("status", c_vp),
         ("total_q", c_i64), ("total_k", c_i64),
+        ("work_counter", c_vp),
     ]
 
 

@@ -21,6 +21,7 @@ _DTYPE_TAG = {torch.float32: _capi.QF_F32, torch.float16: _capi.QF_F16,
 _INDEX_TAG = {torch.int32: _capi.QF_I32, torch.int64: _capi.QF_I64}
 
 _status_words: dict[int, torch.Tensor] = {}
+_work_counters: dict[tuple[int, int], torch.Tensor] = {}
 SYNC_CHECK = os.environ.get("TINYSERVER_B200_CHECK", "0") not in ("", "0")
 
 
@@ -66,6 +67,21 @@ def status_word(device: torch.device) -> torch.Tensor:
     if w is None:
         w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
         _status_words[idx] = w
+    return w
+
+
+def work_counter(device: torch.device) -> torch.Tensor:
+    """Two int32 words for the persistent prefill attention kernel, one pair
+    per (device, current stream).  Zero when made; each call claims its work
+    items from it and leaves it at zero when it completes, so calls queued in
+    order on one stream share a pair, and calls on other streams, which may
+    overlap on the GPU, get pairs of their own."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, stream_ptr(torch.device("cuda", idx)))
+    w = _work_counters.get(key)
+    if w is None:
+        w = torch.zeros(2, dtype=torch.int32, device=torch.device("cuda", idx))
+        _work_counters[key] = w
     return w
 
 

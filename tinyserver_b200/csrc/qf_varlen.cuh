@@ -22,6 +22,7 @@ struct VarlenDev {
     float scale;
     int32_t* status;
     int64_t total_q, total_k;  // rows of q and of k / v
+    int32_t* work_counter;     // tcgen05 path: persistent CTAs claim items here
 };
 
 // The tcgen05 kernel (head_dim 128, 16-bit types).  bf16: 1 for bfloat16, 0

@@ -369,6 +369,7 @@ extern "C" int qf_varlen_attention(const qf_varlen_attention_args* p, cudaStream
     a.status = g.status;
     a.total_q = g.total_q;
     a.total_k = g.total_k;
+    a.work_counter = g.work_counter;
     const int max_q = (int)std::min<int64_t>(g.max_seqlen_q, 1 << 30);
     switch (g.dtype) {
     case QF_F32: return qf::dispatch_varlen<float>(a, g.head_dim, max_q, stream);

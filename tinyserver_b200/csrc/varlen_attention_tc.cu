@@ -118,8 +118,11 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                  : "memory");
 }
 
-// Bounded wait for the completion of phase `parity`; false when it ran out.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Bounded wait for the completion of phase `parity`.  False when it ran out
+// (the first wait to run out raises *abort) or, for a wait that watches
+// `abort`, as soon as another wait has raised it: every role then leaves its
+// loop without waiting out each remaining phase.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
     const long long t0 = clock64();
     while (true) {
         uint32_t done;
@@ -131,7 +134,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
             : "r"(smem_u32(bar)), "r"(parity)
             : "memory");
         if (done) return true;
-        if (clock64() - t0 > kWaitCycles) return false;
+        if (abort && *abort) return false;
+        if (clock64() - t0 > kWaitCycles) {
+            if (abort) *abort = 1;
+            return false;
+        }
     }
 }
 
@@ -247,44 +254,80 @@ __device__ __forceinline__ void issue_s(uint32_t tmem, uint32_t ubase, int t, in
 }
 
 struct TcBars {
-    uint64_t q_full;
+    uint64_t q_full, q_empty;
     uint64_t k_full[2], v_full[2], k_empty[2], v_empty[2];
-    uint64_t s_full[2], p_full[2];
-    uint64_t o_final;
+    uint64_t s_full[2], p_full[2], o_final[2];
+    uint64_t item_full[2], item_empty[2];
+    uint64_t drain;
 };
 
+// Readers of each published work item: the V producer, the MMA thread and the
+// eight softmax warps (one arrival per warp).
+constexpr int kItemReaders = 10;
+
+// One work item: 256 queries (two 128-row tiles) of one sequence and query
+// head.  nblk < 0: the tile pair holds no query row.
+struct Item {
+    int hq, hk, q0, q_len, m0, k0, k_len, nb0, nb1, nblk;
+};
+
+// Items are numbered heaviest first for causal attention: every (sequence,
+// head) pair of the last 256-query tile row, then the row before it, ...
+__device__ __forceinline__ Item decode_item(const VarlenDev& a, int it, int ny) {
+    const int nbh = a.batch * a.Hq;
+    const int y = it / nbh, x = it - y * nbh;
+    const int b = x / a.Hq;
+    Item w;
+    w.hq = x - b * a.Hq;
+    w.hk = w.hq / (a.Hq / a.Hkv);
+    w.q0 = __ldg(a.cu_q + b);
+    w.q_len = __ldg(a.cu_q + b + 1) - w.q0;
+    w.m0 = (ny - 1 - y) * 2 * kRows;
+    w.k0 = __ldg(a.cu_k + b);
+    w.k_len = __ldg(a.cu_k + b + 1) - w.k0;
+    w.nb0 = w.nb1 = 0;
+    w.nblk = -1;
+    if (w.m0 >= w.q_len) return w;
+    int nbx[2];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {  // key blocks per tile (tile 1 may hold no rows)
+        const int r0 = w.m0 + t * kRows;
+        const int kend = r0 >= w.q_len ? 0 : a.causal ? min(w.k_len, r0 + kRows) : w.k_len;
+        nbx[t] = (kend + kRows - 1) / kRows;
+    }
+    w.nb0 = nbx[0];
+    w.nb1 = nbx[1];
+    w.nblk = max(nbx[0], nbx[1]);
+    return w;
+}
+
+// Persistent when `work` is given: gridDim.x CTAs (one per SM) claim items
+// from the counter work[0] (heaviest first, so the last items to finish are
+// short ones), and the last CTA to finish, counted in work[1], sets both
+// words back to zero for the next call.  Without `work`, CTA i does item i.
+//
+// The TMA warp's lane 0 claims items and publishes each in a two-slot ring
+// (item_slot / item_full / item_empty) for the other roles, then loads its Q
+// tiles and K blocks; barrier phases run on across items (counters of items,
+// key blocks and tile blocks, kept alike by every role).  While one item's
+// last blocks and its epilogue run, the next item's Q, K and V are loaded and
+// its first S is computed.
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     varlen_attn_tc_kernel(const VarlenDev a, const __grid_constant__ CUtensorMap tq,
                           const __grid_constant__ CUtensorMap tk,
-                          const __grid_constant__ CUtensorMap tv) {
+                          const __grid_constant__ CUtensorMap tv, int ny, int total,
+                          int* work) {
     using P = Packed<T>;
     extern __shared__ __align__(1024) char dsm[];
     __shared__ TcBars bars;
     __shared__ uint32_t tmem_slot;
-    __shared__ int failed;
+    __shared__ int item_slot[2];
+    __shared__ int abort_flag;
+    volatile int* abort = &abort_flag;
+    volatile int* slots = item_slot;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // CTAs are dispatched in block order, x fastest: every (sequence, head) pair
-    // of the last query tile first, then the tile before it, ... -- for causal
-    // attention the longest work first
-    const int b = (int)blockIdx.x / a.Hq, hq = (int)blockIdx.x % a.Hq;
-    const int ctile = (int)gridDim.y - 1 - (int)blockIdx.y;
-    const int q0 = __ldg(a.cu_q + b), q_len = __ldg(a.cu_q + b + 1) - q0;
-    const int m0 = ctile * 2 * kRows;
-    if (m0 >= q_len) return;  // the whole CTA leaves before any barrier
-    const int k0 = __ldg(a.cu_k + b), k_len = __ldg(a.cu_k + b + 1) - k0;
-    const int hk = hq / (a.Hq / a.Hkv);
-    // key blocks per tile (tile 1 may hold no rows)
-    int nbx[2];
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-        const int r0 = m0 + t * kRows;
-        const int kend = r0 >= q_len ? 0 : a.causal ? min(k_len, r0 + kRows) : k_len;
-        nbx[t] = (kend + kRows - 1) / kRows;
-    }
-    const int nb0 = nbx[0], nb1 = nbx[1];
-    const int nblk = max(nb0, nb1);
 
     // operand tiles at 1024-byte aligned offsets: Q_t at t, K_s at 2 + s, V_s at 4 + s
     const uint32_t raw = smem_u32(dsm);
@@ -293,6 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (tid == 0) {
         mbar_init(&bars.q_full, 1);
+        mbar_init(&bars.q_empty, 1);
         for (int s = 0; s < 2; ++s) {
             mbar_init(&bars.k_full[s], 1);
             mbar_init(&bars.v_full[s], 1);
@@ -300,9 +344,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars.v_empty[s], 1);
             mbar_init(&bars.s_full[s], 1);
             mbar_init(&bars.p_full[s], kRows);
+            mbar_init(&bars.o_final[s], 1);
+            mbar_init(&bars.item_full[s], 1);
+            mbar_init(&bars.item_empty[s], kItemReaders);
         }
-        mbar_init(&bars.o_final, 1);
-        failed = 0;
+        mbar_init(&bars.drain, 1);
+        abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == kMmaWarp) {
@@ -318,191 +365,272 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = tmem_slot;
 
     if (warp == kTmaWarp) {
-        // ---- producers: lane 0 loads Q, then the K blocks; lane 1 the V blocks.
-        // A K stage is refilled once the S MMAs that read it are done, a V
-        // stage once the P V MMAs are (two rings, so K runs ahead of V).
-        if (lane < 2 && nblk > 0) {
-            bool ok = true;
-            if (lane == 0) {
-                const int ntile = nb1 > 0 ? 2 : 1;
+        if (lane == 0) {
+            // ---- scheduler + Q / K producer.  A K stage is refilled once the
+            // S MMAs that read it are done, Q once the item's last S MMAs are.
+            uint32_t n = 0, nq = 0, g = 0;  // items published, items loaded, K blocks
+            int next = work ? atomicAdd(work, 1) : (int)blockIdx.x;
+            while (true) {
+                const int slot = (int)(n & 1);
+                if (n >= 2 && !mbar_wait(&bars.item_empty[slot], ((n - 2) >> 1) & 1, abort)) break;
+                int it = next;
+                Item w;
+                w.nblk = -1;
+                while (it < total) {  // skip tile pairs past their sequence's end
+                    w = decode_item(a, it, ny);
+                    if (w.nblk >= 0) break;
+                    it = work ? atomicAdd(work, 1) : total;
+                }
+                const bool done = it >= total;
+                // claim the following item now: its index is back by the time
+                // this one's blocks are queued
+                if (!done) next = work ? atomicAdd(work, 1) : total;
+                slots[slot] = done ? -1 : it;
+                mbar_arrive(&bars.item_full[slot]);
+                ++n;
+                if (done) break;
+                if (w.nblk == 0) continue;  // no keys: nothing to load
+                if (nq > 0) mbar_wait(&bars.q_empty, (nq - 1) & 1, abort);
+                const int ntile = w.nb1 > 0 ? 2 : 1;
                 mbar_expect_tx(&bars.q_full, (uint32_t)(ntile * kTile));
                 for (int t = 0; t < ntile; ++t)
-                    tma_tile(base + t * kTile, &tq, hq, q0 + m0 + t * kRows, &bars.q_full);
+                    tma_tile(base + t * kTile, &tq, w.hq, w.q0 + w.m0 + t * kRows, &bars.q_full);
+                ++nq;
+                for (int j = 0; j < w.nblk; ++j, ++g) {
+                    const int s = (int)(g & 1);
+                    if (g >= 2) mbar_wait(&bars.k_empty[s], ((g - 2) >> 1) & 1, abort);
+                    mbar_expect_tx(&bars.k_full[s], (uint32_t)kTile);
+                    tma_tile(base + (2 + s) * kTile, &tk, w.hk, w.k0 + j * kRows, &bars.k_full[s]);
+                }
             }
-            for (int j = 0; j < nblk; ++j) {
-                const int s = j & 1;
-                uint64_t* empty = lane == 0 ? &bars.k_empty[s] : &bars.v_empty[s];
-                uint64_t* full = lane == 0 ? &bars.k_full[s] : &bars.v_full[s];
-                if (j >= 2) ok &= mbar_wait(empty, (uint32_t)(((j - 2) >> 1) & 1));
-                mbar_expect_tx(full, (uint32_t)kTile);
-                tma_tile(base + ((lane == 0 ? 2 : 4) + s) * kTile, lane == 0 ? &tk : &tv, hk,
-                         k0 + j * kRows, full);
+            // every copy issued has landed before the CTA can leave
+            if (nq > 0) mbar_wait(&bars.q_full, (nq - 1) & 1, nullptr);
+            for (uint32_t d = g > 2 ? g - 2 : 0; d < g; ++d)
+                mbar_wait(&bars.k_full[d & 1], (d >> 1) & 1, nullptr);
+        } else if (lane == 1) {
+            // ---- V producer: a V stage is refilled once its P V MMAs are done
+            uint32_t n = 0, g = 0;
+            while (true) {
+                const int slot = (int)(n & 1);
+                if (!mbar_wait(&bars.item_full[slot], (n >> 1) & 1, abort)) break;
+                const int it = slots[slot];
+                mbar_arrive(&bars.item_empty[slot]);
+                ++n;
+                if (it < 0) break;
+                const Item w = decode_item(a, it, ny);
+                for (int j = 0; j < w.nblk; ++j, ++g) {
+                    const int s = (int)(g & 1);
+                    if (g >= 2) mbar_wait(&bars.v_empty[s], ((g - 2) >> 1) & 1, abort);
+                    mbar_expect_tx(&bars.v_full[s], (uint32_t)kTile);
+                    tma_tile(base + (4 + s) * kTile, &tv, w.hk, w.k0 + j * kRows, &bars.v_full[s]);
+                }
             }
-            if (!ok) atomicOr(&failed, 1);
+            for (uint32_t d = g > 2 ? g - 2 : 0; d < g; ++d)
+                mbar_wait(&bars.v_full[d & 1], (d >> 1) & 1, nullptr);
         }
     } else if (warp == kMmaWarp) {
-        // ---- MMA issue: S_0,0 S_1,0 | PV_0,j S_0,j+1 PV_1,j S_1,j+1 | ...
-        if (lane == 0 && nblk > 0) {
+        // ---- MMA issue, per item: S_0,0 S_1,0 | PV_0,j S_0,j+1 PV_1,j S_1,j+1 | ...
+        if (lane == 0) {
             const uint32_t bf = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
             const uint32_t id_qk = idesc(bf, 0u), id_pv = idesc(bf, 1u);
-            bool ok = mbar_wait(&bars.q_full, 0u);
-            ok &= mbar_wait(&bars.k_full[0], 0u);
-            tc_fence_after();
-            issue_s(tmem, ubase, 0, 0, id_qk, &bars.s_full[0]);
-            if (nb1 > 0) issue_s(tmem, ubase, 1, 0, id_qk, &bars.s_full[1]);
-            mma_commit(&bars.k_empty[0]);  // K_0 is free once these are done
-            for (int j = 0; j < nblk; ++j) {
-                const int s = j & 1;
-                ok &= mbar_wait(&bars.v_full[s], (uint32_t)((j >> 1) & 1));
-                if (j + 1 < nblk) ok &= mbar_wait(&bars.k_full[s ^ 1], (uint32_t)(((j + 1) >> 1) & 1));
+            uint32_t n = 0, nq = 0, g = 0, tb0 = 0, tb1 = 0;
+            while (true) {
+                const int slot = (int)(n & 1);
+                if (!mbar_wait(&bars.item_full[slot], (n >> 1) & 1, abort)) break;
+                const int it = slots[slot];
+                mbar_arrive(&bars.item_empty[slot]);
+                ++n;
+                if (it < 0) break;
+                const Item w = decode_item(a, it, ny);
+                const int nb0 = w.nb0, nb1 = w.nb1, nblk = w.nblk;
+                if (nblk == 0) continue;
+                mbar_wait(&bars.q_full, nq & 1, abort);
+                mbar_wait(&bars.k_full[g & 1], (g >> 1) & 1, abort);
+                tc_fence_after();
+                issue_s(tmem, ubase, 0, (int)(g & 1), id_qk, &bars.s_full[0]);
+                if (nb1 > 0) issue_s(tmem, ubase, 1, (int)(g & 1), id_qk, &bars.s_full[1]);
+                mma_commit(&bars.k_empty[g & 1]);  // K of block 0 is free once these are done
+                if (nblk == 1) mma_commit(&bars.q_empty);
+                for (int j = 0; j < nblk; ++j) {
+                    const uint32_t gj = g + (uint32_t)j;
+                    const int s = (int)(gj & 1);
+                    mbar_wait(&bars.v_full[s], (gj >> 1) & 1, abort);
+                    if (j + 1 < nblk) mbar_wait(&bars.k_full[s ^ 1], ((gj + 1) >> 1) & 1, abort);
 #pragma unroll
-                for (int t = 0; t < 2; ++t) {
-                    const int nbt = t ? nb1 : nb0;
-                    if (j >= nbt) continue;
-                    ok &= mbar_wait(&bars.p_full[t], (uint32_t)(j & 1));
-                    tc_fence_after();
-                    const uint32_t o = tmem + 256u + (uint32_t)(t * kRows);
-                    const uint32_t p = tmem + (uint32_t)(t * kRows);
-                    const uint32_t v = ubase + (uint32_t)((4 + s) * kTile);
+                    for (int t = 0; t < 2; ++t) {
+                        const int nbt = t ? nb1 : nb0;
+                        if (j >= nbt) continue;
+                        mbar_wait(&bars.p_full[t], ((t ? tb1 : tb0) + (uint32_t)j) & 1, abort);
+                        tc_fence_after();
+                        const uint32_t o = tmem + 256u + (uint32_t)(t * kRows);
+                        const uint32_t p = tmem + (uint32_t)(t * kRows);
+                        const uint32_t v = ubase + (uint32_t)((4 + s) * kTile);
 #pragma unroll
-                    for (int k = 0; k < 8; ++k)  // keys in steps of 16
-                        mma_ts(o, p + 8u * k, sdesc(v + k * 2048, kSlab, 1024), id_pv,
-                               (j > 0 || k > 0) ? 1u : 0u);
-                    if (j + 1 < nbt) issue_s(tmem, ubase, t, s ^ 1, id_qk, &bars.s_full[t]);
+                        for (int k = 0; k < 8; ++k)  // keys in steps of 16
+                            mma_ts(o, p + 8u * k, sdesc(v + k * 2048, kSlab, 1024), id_pv,
+                                   (j > 0 || k > 0) ? 1u : 0u);
+                        if (j + 1 < nbt) issue_s(tmem, ubase, t, s ^ 1, id_qk, &bars.s_full[t]);
+                    }
+                    mma_commit(&bars.v_empty[s]);                        // V_j read
+                    if (j + 1 < nblk) mma_commit(&bars.k_empty[s ^ 1]);  // K_j+1 read
+                    if (j + 2 == nblk) mma_commit(&bars.q_empty);        // the last S issued
                 }
-                mma_commit(&bars.v_empty[s]);                     // V_j read
-                if (j + 1 < nblk) mma_commit(&bars.k_empty[s ^ 1]);  // K_j+1 read
+                mma_commit(&bars.o_final[0]);
+                if (nb1 > 0) mma_commit(&bars.o_final[1]);
+                g += (uint32_t)nblk;
+                tb0 += (uint32_t)nb0;
+                tb1 += (uint32_t)nb1;
+                ++nq;
             }
-            mma_commit(&bars.o_final);
-            if (!ok) atomicOr(&failed, 1);
+            // every MMA issued has completed before the CTA can leave
+            mma_commit(&bars.drain);
+            mbar_wait(&bars.drain, 0u, nullptr);
         }
     } else {
         // ---- softmax of tile t, one query row per thread
         const int t = warp >> 2;
-        const int nbt = t ? nb1 : nb0;
         const int r = tid & (kRows - 1);
-        const int qi = m0 + t * kRows + r;  // query row within the sequence
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
         const uint32_t sS = tmem + lane_base + (uint32_t)(t * kRows);
         const uint32_t sO = tmem + lane_base + 256u + (uint32_t)(t * kRows);
         const float sl2 = a.scale * 1.4426950408889634f;  // scores in log2 units
-        float m = -INFINITY, l = 0.f;  // running max (log2 units) and sum
-        bool ok = true;
+        constexpr int64_t ES = sizeof(T);
+        uint32_t n = 0, tbs = 0, nit = 0;  // items read, tile blocks, items with keys
         uint32_t sr[64];  // 32 used in the loop, 64 in the epilogue
-        for (int j = 0; j < nbt; ++j) {
-            ok &= mbar_wait(&bars.s_full[t], (uint32_t)(j & 1));
-            tc_fence_after();
-            const int kb = j * kRows;
-            // masking only on the blocks that reach past the sequence or the diagonal
-            const bool edge = kb + kRows > k_len || (a.causal && kb + kRows - 1 > m0 + t * kRows);
-            const int klim = a.causal ? min(k_len, qi + 1) : k_len;  // keys [kb, klim) count
-            // pass 1: the block's row max, S read in 32-column quarters with the
-            // next quarter in flight, four independent three-input max chains
-            // (sl2 > 0: the launcher sends other scales to the mma.sync kernel)
-            const int lim = klim - kb;  // columns [lim, 128) are masked
-            float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
-            tmem_ld32(sS, sr);
-            tmem_wait_ld();
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                uint32_t nx[32];
-                if (q < 3) tmem_ld32(sS + 32 * (q + 1), nx);
-                if (edge) {
-#pragma unroll
-                    for (int e = 0; e < 32; ++e)
-                        if (32 * q + e >= lim) sr[e] = __float_as_uint(-INFINITY);
-                }
-#pragma unroll
-                for (int e = 0; e < 32; e += 8) {
-                    mx0 = max3(mx0, __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]));
-                    mx1 = max3(mx1, __uint_as_float(sr[e + 2]), __uint_as_float(sr[e + 3]));
-                    mx2 = max3(mx2, __uint_as_float(sr[e + 4]), __uint_as_float(sr[e + 5]));
-                    mx3 = max3(mx3, __uint_as_float(sr[e + 6]), __uint_as_float(sr[e + 7]));
-                }
-                if (q < 3) {
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) sr[e] = nx[e];
-                }
+        while (true) {
+            const int slot = (int)(n & 1);
+            const bool got = mbar_wait(&bars.item_full[slot], (n >> 1) & 1, abort);
+            if (!__all_sync(0xffffffffu, got)) break;
+            const int it = slots[slot];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars.item_empty[slot]);
+            ++n;
+            if (it < 0) break;
+            const Item w = decode_item(a, it, ny);
+            const int nbt = t ? w.nb1 : w.nb0;
+            const int qi = w.m0 + t * kRows + r;  // query row within the sequence
+            T* out = reinterpret_cast<T*>(a.out + ((int64_t)(w.q0 + qi) * a.ot +
+                                                   (int64_t)w.hq * a.oh) * ES);
+            if (nbt == 0) {
+                if (qi < w.q_len)  // no keys: 0 / 0, as the reference's acc / l
+                    for (int d = 0; d < 128; ++d) out[d] = Dt<T>::from_f(__int_as_float(0x7fc00000));
+                continue;
             }
-            const float mx = max3(mx0, mx1, fmaxf(mx2, mx3)) * sl2;
-            // the reference max moves only when the row max grows by more than
-            // 2^8: until then p stays below 256 and O needs no rescaling; the
-            // result O / l is the same either way
-            float corr = 1.f;
-            if (mx > m + 8.f) {
-                corr = m == -INFINITY ? 0.f : ex2(m - mx);
-                m = mx;
-            }
-            const bool grow = j > 0 && corr != 1.f;
-            if (__any_sync(0xffffffffu, grow)) {  // this warp's rows of O_t
-                const float f = grow ? corr : 1.f;
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t o[32];
-                    tmem_ld32(sO + 32 * c, o);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-                    tmem_st32(sO + 32 * c, o);
-                }
-            }
-            const float mref = m == -INFINITY ? 0.f : m;  // a row with no key yet: every p is 0
-            // pass 2: p = 2^(s * scale * log2e - m), rounded to the value dtype and
-            // packed in pairs, quarter by quarter; each quarter's P goes over S
-            // columns [16q, 16q + 16), already read; the row sum in two packed
-            // accumulator pairs
-            float ps0 = 0.f, ps1 = 0.f, ps2 = 0.f, ps3 = 0.f;
-            uint32_t pk[16];
-            tmem_ld32(sS, sr);
-            tmem_wait_ld();
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                uint32_t nx[32];
-                if (q < 3) tmem_ld32(sS + 32 * (q + 1), nx);
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const int c0 = 32 * q + 2 * e;
-                    float x0, x1;
-                    fma2(x0, x1, __uint_as_float(sr[2 * e]), __uint_as_float(sr[2 * e + 1]), sl2,
-                         -mref);
+            const int klim = a.causal ? min(w.k_len, qi + 1) : w.k_len;  // keys [0, klim) count
+            float m = -INFINITY, l = 0.f;  // running max (log2 units) and sum
+            for (int j = 0; j < nbt; ++j) {
+                mbar_wait(&bars.s_full[t], (tbs + (uint32_t)j) & 1, abort);
+                tc_fence_after();
+                const int kb = j * kRows;
+                // masking only on the blocks that reach past the sequence or the diagonal
+                const bool edge =
+                    kb + kRows > w.k_len || (a.causal && kb + kRows - 1 > w.m0 + t * kRows);
+                // pass 1: the block's row max, S read in 32-column quarters with the
+                // next quarter in flight, four independent three-input max chains
+                // (sl2 > 0: the launcher sends other scales to the mma.sync kernel)
+                const int lim = klim - kb;  // columns [lim, 128) are masked
+                float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+                tmem_ld32(sS, sr);
+                tmem_wait_ld();
+    #pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    uint32_t nx[32];
+                    if (q < 3) tmem_ld32(sS + 32 * (q + 1), nx);
                     if (edge) {
-                        if (c0 >= lim) x0 = -INFINITY;
-                        if (c0 + 1 >= lim) x1 = -INFINITY;
+    #pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            if (32 * q + e >= lim) sr[e] = __float_as_uint(-INFINITY);
                     }
-                    const float p0 = ex2(x0), p1 = ex2(x1);
-                    if (e & 1)
-                        add2(ps2, ps3, p0, p1);
-                    else
-                        add2(ps0, ps1, p0, p1);
-                    pk[e] = P::pack(p0, p1);
+    #pragma unroll
+                    for (int e = 0; e < 32; e += 8) {
+                        mx0 = max3(mx0, __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]));
+                        mx1 = max3(mx1, __uint_as_float(sr[e + 2]), __uint_as_float(sr[e + 3]));
+                        mx2 = max3(mx2, __uint_as_float(sr[e + 4]), __uint_as_float(sr[e + 5]));
+                        mx3 = max3(mx3, __uint_as_float(sr[e + 6]), __uint_as_float(sr[e + 7]));
+                    }
+                    if (q < 3) {
+                        tmem_wait_ld();
+    #pragma unroll
+                        for (int e = 0; e < 32; ++e) sr[e] = nx[e];
+                    }
                 }
-                // keys [32q, 32q + 32) -> columns [16q, 16q + 16): read already,
-                // and below the quarter in flight
-                tmem_st16(sS + 16 * q, pk);
-                if (q < 3) {
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) sr[e] = nx[e];
+                const float mx = max3(mx0, mx1, fmaxf(mx2, mx3)) * sl2;
+                // the reference max moves only when the row max grows by more than
+                // 2^8: until then p stays below 256 and O needs no rescaling; the
+                // result O / l is the same either way
+                float corr = 1.f;
+                if (mx > m + 8.f) {
+                    corr = m == -INFINITY ? 0.f : ex2(m - mx);
+                    m = mx;
                 }
+                const bool grow = j > 0 && corr != 1.f;
+                if (__any_sync(0xffffffffu, grow)) {  // this warp's rows of O_t
+                    const float f = grow ? corr : 1.f;
+    #pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t o[32];
+                        tmem_ld32(sO + 32 * c, o);
+                        tmem_wait_ld();
+    #pragma unroll
+                        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+                        tmem_st32(sO + 32 * c, o);
+                    }
+                }
+                const float mref = m == -INFINITY ? 0.f : m;  // a row with no key yet: every p is 0
+                // pass 2: p = 2^(s * scale * log2e - m), rounded to the value dtype and
+                // packed in pairs, quarter by quarter; each quarter's P goes over S
+                // columns [16q, 16q + 16), already read; the row sum in two packed
+                // accumulator pairs
+                float ps0 = 0.f, ps1 = 0.f, ps2 = 0.f, ps3 = 0.f;
+                uint32_t pk[16];
+                tmem_ld32(sS, sr);
+                tmem_wait_ld();
+    #pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    uint32_t nx[32];
+                    if (q < 3) tmem_ld32(sS + 32 * (q + 1), nx);
+    #pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const int c0 = 32 * q + 2 * e;
+                        float x0, x1;
+                        fma2(x0, x1, __uint_as_float(sr[2 * e]), __uint_as_float(sr[2 * e + 1]), sl2,
+                             -mref);
+                        if (edge) {
+                            if (c0 >= lim) x0 = -INFINITY;
+                            if (c0 + 1 >= lim) x1 = -INFINITY;
+                        }
+                        const float p0 = ex2(x0), p1 = ex2(x1);
+                        if (e & 1)
+                            add2(ps2, ps3, p0, p1);
+                        else
+                            add2(ps0, ps1, p0, p1);
+                        pk[e] = P::pack(p0, p1);
+                    }
+                    // keys [32q, 32q + 32) -> columns [16q, 16q + 16): read already,
+                    // and below the quarter in flight
+                    tmem_st16(sS + 16 * q, pk);
+                    if (q < 3) {
+                        tmem_wait_ld();
+    #pragma unroll
+                        for (int e = 0; e < 32; ++e) sr[e] = nx[e];
+                    }
+                }
+                l = l * corr + ((ps0 + ps1) + (ps2 + ps3));
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&bars.p_full[t]);
             }
-            l = l * corr + ((ps0 + ps1) + (ps2 + ps3));
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(&bars.p_full[t]);
-        }
-        if (nbt > 0) {
-            ok &= mbar_wait(&bars.o_final, 0u);
+            tbs += (uint32_t)nbt;
+            mbar_wait(&bars.o_final[t], nit & 1, abort);
+            ++nit;
             tc_fence_after();
-            constexpr int64_t ES = sizeof(T);
-            T* out = reinterpret_cast<T*>(a.out + ((int64_t)(q0 + qi) * a.ot + (int64_t)hq * a.oh) * ES);
             const float inv = 1.f / l;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 tmem_ld32(sO + 64 * h, sr);
                 tmem_ld32(sO + 64 * h + 32, sr + 32);
                 tmem_wait_ld();
-                if (qi < q_len && ok) {
+                if (qi < w.q_len && !*abort) {
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
                         uint4 v;
@@ -514,17 +642,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-        } else if (qi < q_len) {  // no keys: 0 / 0, as the reference's acc / l
-            constexpr int64_t ES = sizeof(T);
-            T* out = reinterpret_cast<T*>(a.out + ((int64_t)(q0 + qi) * a.ot + (int64_t)hq * a.oh) * ES);
-            for (int d = 0; d < 128; ++d) out[d] = Dt<T>::from_f(__int_as_float(0x7fc00000));
+            // the next item's first P V overwrites O: these loads are ordered
+            // before it by the fence ahead of that item's first p_full arrival
         }
-        if (!ok) atomicOr(&failed, 1);
     }
 
     tc_fence_before();
     __syncthreads();
-    if (tid == 0 && failed) flag(a.status, QF_FLAG_TIMEOUT);
+    if (tid == 0) {
+        if (abort_flag) flag(a.status, QF_FLAG_TIMEOUT);
+        if (work) {
+            __threadfence();
+            if (atomicAdd(work + 1, 1) == (int)gridDim.x - 1) {  // the last CTA out
+                atomicExch(work, 0);
+                atomicExch(work + 1, 0);
+            }
+        }
+    }
     if (warp == kMmaWarp) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
@@ -579,10 +713,16 @@ int launch_tc(const VarlenDev& a, int max_q, cudaStream_t stream) {
         !make_map(&tk, a.k, bf, a.Hkv, a.total_k, a.kh, a.kt) ||
         !make_map(&tv, a.v, bf, a.Hkv, a.total_k, a.vh, a.vt))
         return QF_ERR_UNSUPPORTED;
-    if ((int64_t)a.batch * a.Hq >= (int64_t)1 << 31 || ceil_div(max_q, 2 * kRows) > 65535)
-        return QF_ERR_UNSUPPORTED;
-    const dim3 grid((unsigned)(a.batch * a.Hq), (unsigned)ceil_div(max_q, 2 * kRows));
-    kernel<<<grid, kThreads, kSmem, stream>>>(a, tq, tk, tv);
+    // items: (batch x query heads) x 256-query tile rows; every CTA claims
+    // one past the last, so the counter reaches total + grid
+    const int64_t ny = ceil_div(max_q, 2 * kRows);
+    const int64_t total = (int64_t)a.batch * a.Hq * ny;
+    const int64_t sms = sm_count();
+    if (total + sms >= ((int64_t)1 << 31)) return QF_ERR_UNSUPPORTED;
+    if (total == 0) return QF_OK;
+    const int64_t grid = a.work_counter ? std::min<int64_t>(total, sms) : total;
+    kernel<<<(unsigned)grid, kThreads, kSmem, stream>>>(a, tq, tk, tv, (int)ny, (int)total,
+                                                         a.work_counter);
     return check_launch();
 }
 
@@ -592,6 +732,7 @@ int launch_varlen_tc(const VarlenDev& a, int bf16, int max_q, cudaStream_t strea
     if (a.total_q <= 0 || a.total_k <= 0 || a.total_q >= (1ll << 31) || a.total_k >= (1ll << 31))
         return QF_ERR_UNSUPPORTED;
     if (!(a.scale > 0.f) || isinf(a.scale)) return QF_ERR_UNSUPPORTED;  // max(s) * scale is the max
+    if (reinterpret_cast<uintptr_t>(a.work_counter) % alignof(int32_t)) return QF_ERR_INVALID;
     return bf16 ? launch_tc<__nv_bfloat16>(a, max_q, stream) : launch_tc<__half>(a, max_q, stream);
 }
 

@@ -16,7 +16,8 @@ import math
 import torch
 
 from .. import _capi
-from .._runtime import after_op, dtype_tag, require_cuda, status_word, stream_ptr
+from .._runtime import (after_op, dtype_tag, require_cuda, status_word, stream_ptr,
+                        work_counter)
 
 __all__ = ["flash_attn_varlen_func", "paged_attention_forward", "paged_attention_workspace_bytes"]
 
@@ -134,6 +135,7 @@ def flash_attn_varlen_func(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     a.dtype = tag
     a.status = status_word(dev).data_ptr()
     a.total_q, a.total_k = Tq, Tk
+    a.work_counter = work_counter(dev).data_ptr()
     rc = _capi.lib().qf_varlen_attention(a, stream_ptr(dev))
     _capi.check(rc, "flash_attn_varlen_func")
     after_op(dev)
