@@ -50,7 +50,8 @@ namespace {
 constexpr int kRows = 128;                // rows per tile, keys per block
 constexpr int kSlab = kRows * 128;        // 16 KB
 constexpr int kTile = 2 * kSlab;          // 32 KB: one 128 x 128 tile
-constexpr int kSmem = 6 * kTile + 1024;   // Q[2], K[2], V[2] + alignment slack
+constexpr int kStage = 4096;              // a softmax warp's epilogue staging: 32 rows x 128 B
+constexpr int kSmem = 6 * kTile + 8 * kStage + 1024;  // Q[2], K[2], V[2], staging, alignment
 constexpr int kThreads = 320;
 constexpr int kMmaWarp = 8, kTmaWarp = 9;
 constexpr uint32_t kTmemCols = 512;       // S_0 | S_1 | O_0 | O_1
@@ -469,14 +470,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int k = 0; k < 8; ++k)  // keys in steps of 16
                             mma_ts(o, p + 8u * k, sdesc(v + k * 2048, kSlab, 1024), id_pv,
                                    (j > 0 || k > 0) ? 1u : 0u);
-                        if (j + 1 < nbt) issue_s(tmem, ubase, t, s ^ 1, id_qk, &bars.s_full[t]);
+                        if (j + 1 < nbt)
+                            issue_s(tmem, ubase, t, s ^ 1, id_qk, &bars.s_full[t]);
+                        else  // O_t is final once this tile's MMAs so far are done
+                            mma_commit(&bars.o_final[t]);
                     }
                     mma_commit(&bars.v_empty[s]);                        // V_j read
                     if (j + 1 < nblk) mma_commit(&bars.k_empty[s ^ 1]);  // K_j+1 read
                     if (j + 2 == nblk) mma_commit(&bars.q_empty);        // the last S issued
                 }
-                mma_commit(&bars.o_final[0]);
-                if (nb1 > 0) mma_commit(&bars.o_final[1]);
                 g += (uint32_t)nblk;
                 tb0 += (uint32_t)nb0;
                 tb1 += (uint32_t)nb1;
@@ -509,11 +511,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const Item w = decode_item(a, it, ny);
             const int nbt = t ? w.nb1 : w.nb0;
             const int qi = w.m0 + t * kRows + r;  // query row within the sequence
-            T* out = reinterpret_cast<T*>(a.out + ((int64_t)(w.q0 + qi) * a.ot +
-                                                   (int64_t)w.hq * a.oh) * ES);
             if (nbt == 0) {
-                if (qi < w.q_len)  // no keys: 0 / 0, as the reference's acc / l
+                if (qi < w.q_len) {  // no keys: 0 / 0, as the reference's acc / l
+                    T* out = reinterpret_cast<T*>(
+                        a.out + ((int64_t)(w.q0 + qi) * a.ot + (int64_t)w.hq * a.oh) * ES);
                     for (int d = 0; d < 128; ++d) out[d] = Dt<T>::from_f(__int_as_float(0x7fc00000));
+                }
                 continue;
             }
             const int klim = a.causal ? min(w.k_len, qi + 1) : w.k_len;  // keys [0, klim) count
@@ -624,23 +627,40 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_wait(&bars.o_final[t], nit & 1, abort);
             ++nit;
             tc_fence_after();
+            // O / l, 64 columns at a time: each thread packs its row into the
+            // warp's staging buffer (16-byte chunk c of row r at chunk c ^ r % 8,
+            // no bank conflicts), then the warp writes 4 whole 128-byte row
+            // segments per store instruction
             const float inv = 1.f / l;
+            char* stage = base + 6 * kTile + warp * kStage;
+            const int row0 = w.m0 + t * kRows + (warp & 3) * 32;  // the warp's first row
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 tmem_ld32(sO + 64 * h, sr);
                 tmem_ld32(sO + 64 * h + 32, sr + 32);
                 tmem_wait_ld();
-                if (qi < w.q_len && !*abort) {
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        uint4 v;
-                        v.x = P::pack(__uint_as_float(sr[8 * c]) * inv, __uint_as_float(sr[8 * c + 1]) * inv);
-                        v.y = P::pack(__uint_as_float(sr[8 * c + 2]) * inv, __uint_as_float(sr[8 * c + 3]) * inv);
-                        v.z = P::pack(__uint_as_float(sr[8 * c + 4]) * inv, __uint_as_float(sr[8 * c + 5]) * inv);
-                        v.w = P::pack(__uint_as_float(sr[8 * c + 6]) * inv, __uint_as_float(sr[8 * c + 7]) * inv);
-                        *reinterpret_cast<uint4*>(out + 64 * h + 8 * c) = v;
+                for (int c = 0; c < 8; ++c) {
+                    uint4 v;
+                    v.x = P::pack(__uint_as_float(sr[8 * c]) * inv, __uint_as_float(sr[8 * c + 1]) * inv);
+                    v.y = P::pack(__uint_as_float(sr[8 * c + 2]) * inv, __uint_as_float(sr[8 * c + 3]) * inv);
+                    v.z = P::pack(__uint_as_float(sr[8 * c + 4]) * inv, __uint_as_float(sr[8 * c + 5]) * inv);
+                    v.w = P::pack(__uint_as_float(sr[8 * c + 6]) * inv, __uint_as_float(sr[8 * c + 7]) * inv);
+                    *reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) * 16)) = v;
+                }
+                __syncwarp();
+                const bool write = !*abort;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int rr = 4 * i + (lane >> 3), c = lane & 7;
+                    const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 128 + ((c ^ (rr & 7)) * 16));
+                    if (write && row0 + rr < w.q_len) {
+                        T* dst = reinterpret_cast<T*>(
+                            a.out + ((int64_t)(w.q0 + row0 + rr) * a.ot + (int64_t)w.hq * a.oh) * ES);
+                        *reinterpret_cast<uint4*>(dst + 64 * h + 8 * c) = v;
                     }
                 }
+                __syncwarp();
             }
             // the next item's first P V overwrites O: these loads are ordered
             // before it by the fence ahead of that item's first p_full arrival
