@@ -196,3 +196,21 @@ def test_persistent_schedule_matches_one_cta_per_item(lens):
         tsb.check_errors()
         assert torch.equal(out, one)
         assert counter.tolist() == [0, 0]
+
+
+@pytest.mark.parametrize("scale", [1.0, 3.0])
+def test_large_scores_growing_across_blocks(scale):
+    """Scores whose row max grows by far more than 2^8 (and 2^32) from one
+    128-key block to the next: the one-pass softmax's lazy rescale and its
+    recompute path for rows whose probabilities would overflow."""
+    lens = [700, 300]
+    q, k, v, cu = _packed(lens, 8, 4, 128, torch.bfloat16, seed=int(scale * 10) + 70)
+    # every 128-key block's keys larger than the block before's
+    pos = torch.cat([torch.arange(n) for n in lens])
+    k = (k.float() * (1.0 + (pos // 128).float()).view(-1, 1, 1)).to(torch.bfloat16)
+    expected = oracle.varlen_attention(q, k, v, cu, cu, True, softmax_scale=scale)
+    out = tsb.flash_attn_varlen_func(q.to(DEV), k.to(DEV), v.to(DEV), cu.to(DEV), cu.to(DEV),
+                                     max(lens), max(lens), True, softmax_scale=scale)
+    tsb.check_errors()
+    assert torch.isfinite(out).all()
+    assert_close(out, expected, f"growing scores scale={scale}", min_exact=0.0)

@@ -56,6 +56,7 @@ constexpr int kThreads = 320;
 constexpr int kMmaWarp = 8, kTmaWarp = 9;
 constexpr uint32_t kTmemCols = 512;       // S_0 | S_1 | O_0 | O_1
 constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at the boost clock
+constexpr float kRedoLog2 = 32.f;  // one-pass softmax: p up to 2^32 kept, beyond redone
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -239,6 +240,175 @@ __device__ __forceinline__ void tmem_wait_ld() {
 }
 __device__ __forceinline__ void tmem_wait_st() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 16 consecutive columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+// This warp's rows of O_t times f (each thread its own row; 1 keeps it).
+__device__ __forceinline__ void scale_o(uint32_t sO, float f) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(sO + 32 * c, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+        tmem_st32(sO + 32 * c, o);
+    }
+}
+
+// Columns [lim, 128) of a 32-column quarter starting at column c0 set to -inf.
+__device__ __forceinline__ void mask_quarter(uint32_t* sr, int c0, int lim) {
+#pragma unroll
+    for (int e = 0; e < 32; ++e)
+        if (c0 + e >= lim) sr[e] = __float_as_uint(-INFINITY);
+}
+
+// The row max of S (raw scores, masked), S read in 32-column quarters with the
+// next quarter in flight, four independent three-input max chains.
+__device__ __forceinline__ float row_max(uint32_t sS, bool edge, int lim, uint32_t* sr) {
+    float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+    tmem_ld32(sS, sr);
+    tmem_wait_ld();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint32_t nx[32];
+        if (q < 3) tmem_ld32(sS + 32 * (q + 1), nx);
+        if (edge) mask_quarter(sr, 32 * q, lim);
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+            mx0 = max3(mx0, __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]));
+            mx1 = max3(mx1, __uint_as_float(sr[e + 2]), __uint_as_float(sr[e + 3]));
+            mx2 = max3(mx2, __uint_as_float(sr[e + 4]), __uint_as_float(sr[e + 5]));
+            mx3 = max3(mx3, __uint_as_float(sr[e + 6]), __uint_as_float(sr[e + 7]));
+        }
+        if (q < 3) {
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) sr[e] = nx[e];
+        }
+    }
+    return max3(mx0, mx1, fmaxf(mx2, mx3));
+}
+
+// p = 2^(s * sl2 - mref) for the 128 columns of S, rounded to T and packed in
+// pairs, quarter by quarter; each quarter's P goes over S columns
+// [16q, 16q + 16), read already and below the quarter in flight.  Returns
+// the row sum of p (two packed accumulator pairs), and in *mx the row max of
+// the raw scores (four three-input max chains).
+template <typename T>
+__device__ __forceinline__ float p_pass(uint32_t sS, float sl2, float mref, bool edge, int lim,
+                                        uint32_t* sr, float* mx) {
+    using P = Packed<T>;
+    float ps0 = 0.f, ps1 = 0.f, ps2 = 0.f, ps3 = 0.f;
+    float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+    uint32_t pk[16];
+    tmem_ld32(sS, sr);
+    tmem_wait_ld();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint32_t nx[32];
+        if (q < 3) tmem_ld32(sS + 32 * (q + 1), nx);
+        if (edge) mask_quarter(sr, 32 * q, lim);  // -inf * sl2 - mref = -inf: p = 0
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+            mx0 = max3(mx0, __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]));
+            mx1 = max3(mx1, __uint_as_float(sr[e + 2]), __uint_as_float(sr[e + 3]));
+            mx2 = max3(mx2, __uint_as_float(sr[e + 4]), __uint_as_float(sr[e + 5]));
+            mx3 = max3(mx3, __uint_as_float(sr[e + 6]), __uint_as_float(sr[e + 7]));
+        }
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            float x0, x1;
+            fma2(x0, x1, __uint_as_float(sr[2 * e]), __uint_as_float(sr[2 * e + 1]), sl2, -mref);
+            const float p0 = ex2(x0), p1 = ex2(x1);
+            if (e & 1)
+                add2(ps2, ps3, p0, p1);
+            else
+                add2(ps0, ps1, p0, p1);
+            pk[e] = P::pack(p0, p1);
+        }
+        tmem_st16(sS + 16 * q, pk);
+        if (q < 3) {
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) sr[e] = nx[e];
+        }
+    }
+    *mx = max3(mx0, mx1, fmaxf(mx2, mx3));
+    return (ps0 + ps1) + (ps2 + ps3);
+}
+
+// q_r . k_c in fp32 on the CUDA cores (head_dim 128).
+template <typename T>
+__device__ __forceinline__ float dot128(const T* q, const T* k) {
+    float acc = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < 128; d += 8) {
+        const uint4 qa = *reinterpret_cast<const uint4*>(q + d);
+        const uint4 ka = *reinterpret_cast<const uint4*>(k + d);
+        const T* qe = reinterpret_cast<const T*>(&qa);
+        const T* ke = reinterpret_cast<const T*>(&ka);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc = fmaf(Dt<T>::to_f(qe[i]), Dt<T>::to_f(ke[i]), acc);
+    }
+    return acc;
+}
+
+// The rare path of the one-pass softmax: a row whose block max exceeds its
+// reference max by more than 2^kRedoLog2 had its p computed against a max far
+// too low (large or infinite values), so the block's P is computed again for
+// that row against the block's own max -- its scores recomputed on the CUDA
+// cores from q and k in global memory, the tensor-core S being overwritten by
+// P already -- and its O is rescaled before this block's P V.  Rows with
+// `redo` false keep their P (read and written back: the tensor-memory copies
+// are warp-wide).  Called by whole warps.
+struct RowState {
+    float m, l;
+};
+
+template <typename T>
+__device__ __noinline__ RowState redo_rows(const T* qp, const char* kp0, int64_t k_bytes, int lim,
+                                           bool redo, uint32_t sS, uint32_t sO, float sl2,
+                                           RowState st) {
+    using P = Packed<T>;
+    // qp: this row's query; kp0: the block's first key row, k_bytes apart
+    auto kp = [&](int c) { return reinterpret_cast<const T*>(kp0 + (int64_t)c * k_bytes); };
+    const int n = min(lim, kRows);
+    float mnew = -INFINITY;
+    if (redo)
+        for (int c = 0; c < n; ++c) mnew = fmaxf(mnew, dot128(qp, kp(c)));
+    mnew *= sl2;
+    const float corr = redo ? ex2(st.m - mnew) : 1.f;
+    float ps = 0.f;
+    for (int q = 0; q < 4; ++q) {
+        uint32_t pk[16];
+        tmem_ld16(sS + 16 * q, pk);
+        tmem_wait_ld();
+        if (redo) {
+            for (int e = 0; e < 16; ++e) {
+                const int c0 = 32 * q + 2 * e;
+                const float p0 = c0 < n ? ex2(fmaf(dot128(qp, kp(c0)), sl2, -mnew)) : 0.f;
+                const float p1 = c0 + 1 < n ? ex2(fmaf(dot128(qp, kp(c0 + 1)), sl2, -mnew)) : 0.f;
+                ps += p0 + p1;
+                pk[e] = P::pack(p0, p1);
+            }
+        }
+        tmem_st16(sS + 16 * q, pk);
+    }
+    tmem_wait_st();
+    scale_o(sO, corr);
+    if (redo) st = RowState{mnew, st.l * corr + ps};
+    return st;
 }
 
 // S_t = Q_t K_s^T (head_dim in steps of 16), then commit to `bar`.
@@ -497,7 +667,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t sO = tmem + lane_base + 256u + (uint32_t)(t * kRows);
         const float sl2 = a.scale * 1.4426950408889634f;  // scores in log2 units
         constexpr int64_t ES = sizeof(T);
-        uint32_t n = 0, tbs = 0, nit = 0;  // items read, tile blocks, items with keys
+        // items read, blocks of tile 0 and of tile 1 so far, items with keys
+        uint32_t n = 0, tb0 = 0, tb1 = 0, nit = 0;
         uint32_t sr[64];  // 32 used in the loop, 64 in the epilogue
         while (true) {
             const int slot = (int)(n & 1);
@@ -511,6 +682,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const Item w = decode_item(a, it, ny);
             const int nbt = t ? w.nb1 : w.nb0;
             const int qi = w.m0 + t * kRows + r;  // query row within the sequence
+            const uint32_t base0 = tb0, base1 = tb1;  // blocks of each tile before this item
+            tb0 += (uint32_t)w.nb0;
+            tb1 += (uint32_t)w.nb1;
             if (nbt == 0) {
                 if (qi < w.q_len) {  // no keys: 0 / 0, as the reference's acc / l
                     T* out = reinterpret_cast<T*>(
@@ -520,7 +694,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 continue;
             }
             const int klim = a.causal ? min(w.k_len, qi + 1) : w.k_len;  // keys [0, klim) count
-            float m = -INFINITY, l = 0.f;  // running max (log2 units) and sum
+            // running reference max m (log2 units), sum l, and a rescale of O
+            // that the block before left for this one
+            float m = -INFINITY, l = 0.f, pend = 1.f;
+            const uint32_t tbs = t ? base1 : base0;
             for (int j = 0; j < nbt; ++j) {
                 mbar_wait(&bars.s_full[t], (tbs + (uint32_t)j) & 1, abort);
                 tc_fence_after();
@@ -528,102 +705,60 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // masking only on the blocks that reach past the sequence or the diagonal
                 const bool edge =
                     kb + kRows > w.k_len || (a.causal && kb + kRows - 1 > w.m0 + t * kRows);
-                // pass 1: the block's row max, S read in 32-column quarters with the
-                // next quarter in flight, four independent three-input max chains
-                // (sl2 > 0: the launcher sends other scales to the mma.sync kernel)
                 const int lim = klim - kb;  // columns [lim, 128) are masked
-                float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
-                tmem_ld32(sS, sr);
-                tmem_wait_ld();
-    #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    uint32_t nx[32];
-                    if (q < 3) tmem_ld32(sS + 32 * (q + 1), nx);
-                    if (edge) {
-    #pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            if (32 * q + e >= lim) sr[e] = __float_as_uint(-INFINITY);
-                    }
-    #pragma unroll
-                    for (int e = 0; e < 32; e += 8) {
-                        mx0 = max3(mx0, __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]));
-                        mx1 = max3(mx1, __uint_as_float(sr[e + 2]), __uint_as_float(sr[e + 3]));
-                        mx2 = max3(mx2, __uint_as_float(sr[e + 4]), __uint_as_float(sr[e + 5]));
-                        mx3 = max3(mx3, __uint_as_float(sr[e + 6]), __uint_as_float(sr[e + 7]));
-                    }
-                    if (q < 3) {
-                        tmem_wait_ld();
-    #pragma unroll
-                        for (int e = 0; e < 32; ++e) sr[e] = nx[e];
-                    }
-                }
-                const float mx = max3(mx0, mx1, fmaxf(mx2, mx3)) * sl2;
-                // the reference max moves only when the row max grows by more than
-                // 2^8: until then p stays below 256 and O needs no rescaling; the
-                // result O / l is the same either way
+                // the block before's P V is done (S_j was issued after it)
+                if (__any_sync(0xffffffffu, pend != 1.f)) scale_o(sO, pend);
+                pend = 1.f;
+                // A row's first block takes its max first (sl2 > 0: the launcher
+                // sends other scales to the mma.sync kernel).  Later blocks take
+                // one pass: P against the reference max so far, the block max on
+                // the side.  The reference max moves when the row max has grown
+                // by more than 2^8 (O / l is the same either way): l at once, O
+                // at the next block's start (or in 1 / l after the last), when
+                // this block's P V is done.  Growth beyond 2^kRedoLog2 (p
+                // possibly infinite) redoes the row.
+                const bool first = __any_sync(0xffffffffu, m == -INFINITY);
                 float corr = 1.f;
-                if (mx > m + 8.f) {
-                    corr = m == -INFINITY ? 0.f : ex2(m - mx);
-                    m = mx;
+                if (first) {
+                    const float mx = row_max(sS, edge, lim, sr) * sl2;
+                    if (mx > m + 8.f) {
+                        corr = m == -INFINITY ? 0.f : ex2(m - mx);
+                        m = mx;
+                    }
+                    const bool grow = j > 0 && corr != 1.f;
+                    if (__any_sync(0xffffffffu, grow)) scale_o(sO, grow ? corr : 1.f);
                 }
-                const bool grow = j > 0 && corr != 1.f;
-                if (__any_sync(0xffffffffu, grow)) {  // this warp's rows of O_t
-                    const float f = grow ? corr : 1.f;
-    #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        uint32_t o[32];
-                        tmem_ld32(sO + 32 * c, o);
-                        tmem_wait_ld();
-    #pragma unroll
-                        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-                        tmem_st32(sO + 32 * c, o);
+                const float mref = m == -INFINITY ? 0.f : m;  // no key yet: every p is 0
+                float mx;
+                const float ps = p_pass<T>(sS, sl2, mref, edge, lim, sr, &mx);
+                mx *= sl2;
+                // (rows past the sequence, whose O is never stored, are left as they are)
+                const bool redo = !first && qi < w.q_len && mx > m + kRedoLog2;
+                if (__any_sync(0xffffffffu, redo)) {
+                    const RowState st = redo_rows<T>(
+                        reinterpret_cast<const T*>(
+                            a.q + ((int64_t)(w.q0 + qi) * a.qt + (int64_t)w.hq * a.qh) * ES),
+                        a.k + ((int64_t)(w.k0 + kb) * a.kt + (int64_t)w.hk * a.kh) * ES,
+                        a.kt * ES, lim, redo, sS, sO, sl2, RowState{m, l});
+                    m = st.m;
+                    l = st.l;
+                }
+                if (first) {
+                    l = l * corr + ps;
+                } else if (!redo) {
+                    if (mx > m + 8.f) {
+                        corr = ex2(m - mx);
+                        l = (l + ps) * corr;
+                        pend = corr;
+                        m = mx;
+                    } else {
+                        l += ps;
                     }
                 }
-                const float mref = m == -INFINITY ? 0.f : m;  // a row with no key yet: every p is 0
-                // pass 2: p = 2^(s * scale * log2e - m), rounded to the value dtype and
-                // packed in pairs, quarter by quarter; each quarter's P goes over S
-                // columns [16q, 16q + 16), already read; the row sum in two packed
-                // accumulator pairs
-                float ps0 = 0.f, ps1 = 0.f, ps2 = 0.f, ps3 = 0.f;
-                uint32_t pk[16];
-                tmem_ld32(sS, sr);
-                tmem_wait_ld();
-    #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    uint32_t nx[32];
-                    if (q < 3) tmem_ld32(sS + 32 * (q + 1), nx);
-    #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const int c0 = 32 * q + 2 * e;
-                        float x0, x1;
-                        fma2(x0, x1, __uint_as_float(sr[2 * e]), __uint_as_float(sr[2 * e + 1]), sl2,
-                             -mref);
-                        if (edge) {
-                            if (c0 >= lim) x0 = -INFINITY;
-                            if (c0 + 1 >= lim) x1 = -INFINITY;
-                        }
-                        const float p0 = ex2(x0), p1 = ex2(x1);
-                        if (e & 1)
-                            add2(ps2, ps3, p0, p1);
-                        else
-                            add2(ps0, ps1, p0, p1);
-                        pk[e] = P::pack(p0, p1);
-                    }
-                    // keys [32q, 32q + 32) -> columns [16q, 16q + 16): read already,
-                    // and below the quarter in flight
-                    tmem_st16(sS + 16 * q, pk);
-                    if (q < 3) {
-                        tmem_wait_ld();
-    #pragma unroll
-                        for (int e = 0; e < 32; ++e) sr[e] = nx[e];
-                    }
-                }
-                l = l * corr + ((ps0 + ps1) + (ps2 + ps3));
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(&bars.p_full[t]);
             }
-            tbs += (uint32_t)nbt;
             mbar_wait(&bars.o_final[t], nit & 1, abort);
             ++nit;
             tc_fence_after();
@@ -631,7 +766,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // warp's staging buffer (16-byte chunk c of row r at chunk c ^ r % 8,
             // no bank conflicts), then the warp writes 4 whole 128-byte row
             // segments per store instruction
-            const float inv = 1.f / l;
+            const float inv = pend / l;  // a rescale the last block left
             char* stage = base + 6 * kTile + warp * kStage;
             const int row0 = w.m0 + t * kRows + (warp & 3) * 32;  // the warp's first row
 #pragma unroll
