@@ -214,3 +214,27 @@ def test_large_scores_growing_across_blocks(scale):
     tsb.check_errors()
     assert torch.isfinite(out).all()
     assert_close(out, expected, f"growing scores scale={scale}", min_exact=0.0)
+
+
+def test_cuda_graph_replays():
+    """Captured once, replayed several times on new inputs: the persistent
+    kernel's work counter is back at zero after every launch, so replays need
+    no reset and match eager calls bit for bit."""
+    lens = [700, 128, 1500, 3]
+    q, k, v, cu = _packed(lens, 16, 8, 128, torch.bfloat16, seed=90)
+    q, k, v, cu = q.to(DEV), k.to(DEV), v.to(DEV), cu.to(DEV)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        tsb.flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), True)  # warm-up
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = tsb.flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), True)
+    for i in range(3):
+        q.copy_(_packed(lens, 16, 8, 128, torch.bfloat16, seed=91 + i)[0].to(DEV))
+        g.replay()
+        torch.cuda.synchronize()
+        eager = tsb.flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), True)
+        tsb.check_errors()
+        assert torch.equal(out, eager), f"replay {i}"
