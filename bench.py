@@ -696,9 +696,69 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> dict | None:
         m = torch.tensor([ms], device=dev, dtype=torch.float64)
         torch.distributed.all_reduce(m, op=torch.distributed.ReduceOp.MAX)
         ms = float(m.item())
+    flops = sum(4 * D * n * (n + 1) // 2 for n in lens) * Hq
+
+    # end to end: q, k, v and cu_seqlens from pinned host memory, the output
+    # back to pinned host memory, every step
+    e2e = None
+    if not args.no_e2e:
+        hq_, hk_, hv_ = (t.cpu().pin_memory() for t in sets[0])
+        hcu = cu.cpu().pin_memory()
+        dq, dk, dv, dcu = (torch.empty_like(t) for t in (*sets[0], cu))
+        out_h = torch.empty(T, Hq, D, dtype=cfg.dtype).pin_memory()
+
+        def e2e_once():
+            for d, h in ((dq, hq_), (dk, hk_), (dv, hv_), (dcu, hcu)):
+                d.copy_(h, non_blocking=True)
+            out_h.copy_(tsb.flash_attn_varlen_func(dq, dk, dv, dcu, dcu, L, L, causal=True),
+                        non_blocking=True)
+
+        for _ in range(3):
+            e2e_once()
+        torch.cuda.synchronize()
+        n_e2e = max(10, min(args.steps, 20))
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(n_e2e):
+            e2e_once()
+        a1.record()
+        torch.cuda.synchronize()
+        e2e_ms = a0.elapsed_time(a1) / n_e2e
+        e2e = {"value": round(world * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+               "ms_per_step": round(e2e_ms, 4),
+               "h2d_bytes_per_step": int(sum(t.numel() * t.element_size() for t in sets[0])
+                                         + cu.numel() * 4),
+               "d2h_bytes_per_step": T * Hq * D * 2}
     if rank != 0:
         return None
-    flops = sum(4 * D * n * (n + 1) // 2 for n in lens) * Hq
+
+    # CPU baseline: whole sequences of the batch, in order, through the
+    # restatement of the reference's kernel (32-key blocks, torch on the host
+    # cores) for about ten seconds; FLOP rate scaled to the batch
+    cpu = None
+    if not args.no_cpu_baseline and world == 1:  # rank 0 at N=1 only
+        from oracle import oracle
+        cq_h, ck_h, cv_h = (t.cpu() for t in sets[0])
+        offs = [0]
+        for n in lens:
+            offs.append(offs[-1] + n)
+        done, c0, i = 0, time.perf_counter(), 0
+        while True:
+            n, o = lens[i % len(lens)], offs[i % len(lens)]
+            c1 = torch.tensor([0, n], dtype=torch.int32)
+            oracle.varlen_attention(cq_h[o:o + n], ck_h[o:o + n], cv_h[o:o + n], c1, c1, True)
+            done += 4 * D * n * (n + 1) // 2 * Hq
+            i += 1
+            secs = time.perf_counter() - c0
+            if secs > min(args.cpu_seconds, 10.0):
+                break
+        rate = done / secs
+        cpu = {"value": round(T / (flops / rate), 1), "unit": "tokens/s",
+               "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{i} whole sequences of the batch in order ({done / 1e9:.1f} GFLOP in "
+                         f"{secs:.1f} s, {rate / 1e9:.2f} GFLOP/s), scaled to the batch's "
+                         f"{flops / 1e9:.0f} GFLOP; the reference kernel's algorithm restated "
+                         "in torch on the host cores"}
     per_ms = ms / args.steps
     tf = flops / (per_ms * 1e-3) / 1e12
     peak, kind = tensor_peak()
@@ -715,8 +775,8 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> dict | None:
         "roofline": {"bound": "tensor", "kernel": "varlen_attn_tc_kernel", "achieved": round(tf, 1),
                      "peak": peak, "unit": "TFLOP/s", "frac": round(tf / peak, 4),
                      "peak_source": f"{kind} bf16_tflops (cuBLAS burst)", "flops_per_launch": flops,
-                     "traffic": None},
-        "gpu_launches": args.steps, "clocks": clocks,
+                     "traffic": ncu_traffic("varlen_attn_tc_kernel")},
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks,
     }
 
 
