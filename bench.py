@@ -609,10 +609,65 @@ def run_attention(args, rank: int, world: int, local_rank: int) -> dict | None:
         m = torch.tensor([ms], device=dev, dtype=torch.float64)
         torch.distributed.all_reduce(m, op=torch.distributed.ReduceOp.MAX)
         ms = float(m.item())
+
+    # end to end: the step's queries, block tables and lengths from pinned host
+    # memory, the output back; the KV cache is device state, as in the engine
+    e2e = None
+    if not args.no_e2e:
+        hq_, hbt, hsl = q.cpu().pin_memory(), bt.cpu().pin_memory(), sl.cpu().pin_memory()
+        dq, dbt, dsl = torch.empty_like(q), torch.empty_like(bt), torch.empty_like(sl)
+        out_h = torch.empty(S, Hq, D, dtype=cfg.dtype).pin_memory()
+
+        def e2e_once():
+            for d, h in ((dq, hq_), (dbt, hbt), (dsl, hsl)):
+                d.copy_(h, non_blocking=True)
+            out_h.copy_(tsb.paged_attention_forward(dq, pool[0], pool[1], dbt, B, dsl,
+                                                    workspace=ws), non_blocking=True)
+
+        for _ in range(3):
+            e2e_once()
+        torch.cuda.synchronize()
+        n_e2e = max(10, min(args.steps, 50))
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(n_e2e):
+            e2e_once()
+        a1.record()
+        torch.cuda.synchronize()
+        e2e_ms = a0.elapsed_time(a1) / n_e2e
+        e2e = {"value": round(world * S / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+               "ms_per_step": round(e2e_ms, 4),
+               "h2d_bytes_per_step": int(q.numel() * 2 + bt.numel() * bt.element_size()
+                                         + sl.numel() * 4),
+               "d2h_bytes_per_step": S * Hq * D * 2}
     if rank != 0:
         return None
-    peak, peak_kind = hbm_peak()
     ctx = int(lens.sum())
+
+    # CPU baseline: the restated reference kernel on the host cores over
+    # groups of 8 sequences for about ten seconds, scaled to the batch by
+    # context tokens (the work is one K and V row per context token)
+    cpu = None
+    if not args.no_cpu_baseline and world == 1:  # rank 0 at N=1 only
+        from oracle import oracle
+        kc, vc, qh, bth = pool[0].cpu(), pool[1].cpu(), q.cpu(), bt.cpu()
+        done, c0, i = 0, time.perf_counter(), 0
+        while True:
+            lo = (8 * i) % S
+            oracle.paged_attention_decode(qh[lo:lo + 8], kc, vc, bth[lo:lo + 8], B,
+                                          lens[lo:lo + 8])
+            done += int(lens[lo:lo + 8].sum())
+            i += 1
+            secs = time.perf_counter() - c0
+            if secs > min(args.cpu_seconds, 10.0):
+                break
+        rate = done / secs
+        cpu = {"value": round(S / (ctx / rate), 1), "unit": "tokens/s",
+               "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{8 * i} sequences of the batch in groups of 8 ({done} context tokens "
+                         f"in {secs:.1f} s), scaled to the batch's {ctx} context tokens; the "
+                         "reference kernel's algorithm restated in torch on the host cores"}
+    peak, peak_kind = hbm_peak()
     nbytes = ctx * Hkv * D * 2 * 2 + 2 * S * Hq * D * 2 + S * (bt.shape[1] + 1) * 4
     per_ms = ms / args.steps
     gbs = nbytes / (per_ms * 1e-3) / 1e9
@@ -629,7 +684,7 @@ def run_attention(args, rank: int, world: int, local_rank: int) -> dict | None:
                      "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(gbs / peak, 4), "algorithmic_bytes_per_launch": nbytes,
                      "traffic": ncu_traffic("paged_attention")},
-        "gpu_launches": 2 * args.steps, "clocks": clocks,
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 2 * args.steps, "clocks": clocks,
     }
 
 
