@@ -238,3 +238,36 @@ def test_cuda_graph_replays():
         eager = tsb.flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), True)
         tsb.check_errors()
         assert torch.equal(out, eager), f"replay {i}"
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_empty_sequences_keyless_rows_and_many_short(causal):
+    """Edge cases of the packed layout on the tensor-core path: zero-length
+    sequences between others, a sequence whose queries have no keys (0 / 0,
+    NaN rows, as the reference's acc / l), and 600 short sequences (many more
+    work items than SMs, most with one tile)."""
+    g = torch.Generator().manual_seed(120 + causal)
+    lq = [3, 0, 130, 0, 1, 9, 300]
+    lk = [3, 0, 130, 0, 1, 0, 300]  # the sixth sequence: 9 queries, no keys
+    q = torch.randn(sum(lq), 8, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(sum(lk), 2, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(sum(lk), 2, 128, generator=g).to(torch.bfloat16)
+    cq = torch.tensor([0] + torch.tensor(lq).cumsum(0).tolist(), dtype=torch.int32)
+    ck = torch.tensor([0] + torch.tensor(lk).cumsum(0).tolist(), dtype=torch.int32)
+    expected = oracle.varlen_attention(q, k, v, cq, ck, causal)
+    out = tsb.flash_attn_varlen_func(q.to(DEV), k.to(DEV), v.to(DEV), cq.to(DEV), ck.to(DEV),
+                                     max(lq), max(lk), causal).cpu()
+    tsb.check_errors()
+    nan_e, nan_o = torch.isnan(expected.float()), torch.isnan(out.float())
+    assert nan_e.any() and torch.equal(nan_e, nan_o)
+    keep = ~nan_e.flatten(1).any(1)
+    assert_close(out[keep], expected[keep], f"empty / keyless causal={causal}", min_exact=0.0)
+
+    lens = torch.randint(1, 41, (600,), generator=g).tolist()
+    q, k, v, cu = _packed(lens, 8, 2, 128, torch.bfloat16, seed=130 + causal)
+    expected = oracle.varlen_attention(q, k, v, cu, cu, causal)
+    out = tsb.flash_attn_varlen_func(q.to(DEV), k.to(DEV), v.to(DEV), cu.to(DEV), cu.to(DEV),
+                                     max(lens), max(lens), causal)
+    tsb.check_errors()
+    assert_close(out, expected, f"600 short causal={causal}", min_exact=0.0)
+    _as_accurate_as_reference(out, q, k, v, cu, cu, causal, f"600 short causal={causal}")
