@@ -44,6 +44,12 @@ namespace {
 #ifndef QF_SAMPLE_CLUSTER
 #define QF_SAMPLE_CLUSTER 8
 #endif
+#ifndef QF_SAMPLE_LOADS
+#define QF_SAMPLE_LOADS 5  // 16-byte loads in flight per thread: a whole slice in one batch
+#endif
+#ifndef QF_SAMPLE_PREFETCH
+#define QF_SAMPLE_PREFETCH 1  // prefetch into L2 the slice the next wave of clusters reads
+#endif
 
 constexpr int kClusterCtas = QF_SAMPLE_CLUSTER;
 constexpr int kThreads = 512;
@@ -63,6 +69,7 @@ struct SampleDev {
     int64_t vocab;
     int slice;           // elements per CTA, a multiple of 8
     int vec;             // 16-byte loads (aligned rows)
+    int ahead;           // rows between a cluster and the one a wave later (0: no prefetch)
     const float* temperature;
     const void* top_k;
     int top_k_i64;
@@ -180,7 +187,7 @@ __device__ __forceinline__ void load_slice(const SampleDev& a, const T* row, int
                                            float* sv, float& best, uint32_t& best_i) {
     if (a.vec) {
         constexpr int PV = Dt<T>::kPerVec;
-        constexpr int U = 4;  // 16-byte loads in flight per thread
+        constexpr int U = QF_SAMPLE_LOADS;
         const int nv = n / PV;
         for (int c0 = threadIdx.x; c0 < nv; c0 += U * kThreads) {
             uint4 raw[U];
@@ -582,6 +589,17 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleDev a) 
     const int64_t left = a.vocab - base;
     const int n = left <= 0 ? 0 : (left < a.slice ? (int)left : a.slice);
     const T* lrow = reinterpret_cast<const T*>(a.logits) + row * a.row_stride + base;
+    // Rows run one cluster each, about `ahead` clusters at a time, in row
+    // order: the cluster that takes row + ahead starts when one of this wave
+    // ends, so its slice is fetched into L2 now, one bulk prefetch per CTA.
+    if (QF_SAMPLE_PREFETCH && threadIdx.x == 0 && a.vec && a.ahead > 0 && n > 0 &&
+        row + a.ahead < (int64_t)(gridDim.x / kClusterCtas)) {
+        const uint32_t bytes = (uint32_t)(((int64_t)n * (int64_t)sizeof(T)) & ~(int64_t)15);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                         reinterpret_cast<uint64_t>(lrow + a.ahead * a.row_stride)),
+                     "r"(bytes)
+                     : "memory");
+    }
 
     const float temp = a.temperature[row];
     const float tc = fmaxf(temp, 1e-5f);
@@ -767,7 +785,22 @@ int launch_sample(const SampleDev& a, int64_t batch, cudaStream_t stream) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, a);
+    // clusters resident at once for this slice size (queried once per size)
+    static std::atomic<int64_t> wave_key{-1};
+    static std::atomic<int> wave{0};
+    const int64_t key = (int64_t)smem;
+    if (wave_key.load(std::memory_order_relaxed) != key) {
+        int nc = 0;
+        if (cudaOccupancyMaxActiveClusters(&nc, kernel, &cfg) != cudaSuccess) {
+            (void)cudaGetLastError();
+            nc = 0;
+        }
+        wave.store(nc, std::memory_order_relaxed);
+        wave_key.store(key, std::memory_order_relaxed);
+    }
+    SampleDev b = a;
+    b.ahead = wave.load(std::memory_order_relaxed);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, b);
     return e == cudaSuccess ? QF_OK : launch_failed(e);
 }
 
