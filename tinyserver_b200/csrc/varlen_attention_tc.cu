@@ -8,8 +8,10 @@
 // h / (Hq / Hkv), fp32 softmax, probabilities rounded to the value dtype
 // before they meet V (:121) -- for head_dim 128 in bf16 / fp16.
 //
-// One CTA per (256 queries = two 128-row tiles, sequence, query head), ten
-// warps:
+// A work item is two 128-row query tiles of one sequence that read the same
+// K and V: the same rows of two query heads of one GQA group when the group
+// size is even, else 256 consecutive rows of one head.  Persistent CTAs (one
+// per SM) take items in turn; each has ten warps:
 //   warps 0-3   softmax of tile 0 (thread t owns query row t: tensor-memory
 //               lane t), warps 4-7 the same for tile 1;
 //   warp 8      issues the MMAs (one thread);
@@ -436,33 +438,49 @@ struct TcBars {
 // eight softmax warps (one arrival per warp).
 constexpr int kItemReaders = 10;
 
-// One work item: 256 queries (two 128-row tiles) of one sequence and query
-// head.  nblk < 0: the tile pair holds no query row.
+// Two query tiles share each work item's K and V blocks.  When query heads
+// come in pairs per KV head (an even group size Hq / Hkv), a tile pair is the
+// same 128 query rows of two heads of one group: both tiles see the same keys,
+// so they have the same number of key blocks and the same causal diagonal and
+// alternate evenly to the end.  Otherwise a tile pair is 256 consecutive query
+// rows of one head.
+__device__ __forceinline__ bool head_pairs(const VarlenDev& a) {
+    return ((a.Hq / a.Hkv) & 1) == 0;
+}
+
+// One work item: two 128-row query tiles of one sequence, tile t at query row
+// r_t of head h_t.  nblk < 0: the item holds no query row.
 struct Item {
-    int hq, hk, q0, q_len, m0, k0, k_len, nb0, nb1, nblk;
+    int h0, h1, r0, r1;  // tiles' query heads and first rows within the sequence
+    int hk, q0, q_len, k0, k_len, nb0, nb1, nblk;
 };
 
 // Items are numbered heaviest first for causal attention: every (sequence,
-// head) pair of the last 256-query tile row, then the row before it, ...
+// head or head pair) of the last tile row, then the row before it, ...
 __device__ __forceinline__ Item decode_item(const VarlenDev& a, int it, int ny) {
-    const int nbh = a.batch * a.Hq;
+    const bool pair = head_pairs(a);
+    const int hx = pair ? a.Hq / 2 : a.Hq;  // head units per sequence
+    const int nbh = a.batch * hx;
     const int y = it / nbh, x = it - y * nbh;
-    const int b = x / a.Hq;
+    const int b = x / hx, u = x - b * hx;
+    const int m0 = (ny - 1 - y) * (pair ? kRows : 2 * kRows);
     Item w;
-    w.hq = x - b * a.Hq;
-    w.hk = w.hq / (a.Hq / a.Hkv);
+    w.h0 = pair ? 2 * u : u;
+    w.h1 = pair ? 2 * u + 1 : u;
+    w.r0 = m0;
+    w.r1 = pair ? m0 : m0 + kRows;
+    w.hk = w.h0 / (a.Hq / a.Hkv);
     w.q0 = __ldg(a.cu_q + b);
     w.q_len = __ldg(a.cu_q + b + 1) - w.q0;
-    w.m0 = (ny - 1 - y) * 2 * kRows;
     w.k0 = __ldg(a.cu_k + b);
     w.k_len = __ldg(a.cu_k + b + 1) - w.k0;
     w.nb0 = w.nb1 = 0;
     w.nblk = -1;
-    if (w.m0 >= w.q_len) return w;
+    if (w.r0 >= w.q_len) return w;
     int nbx[2];
 #pragma unroll
     for (int t = 0; t < 2; ++t) {  // key blocks per tile (tile 1 may hold no rows)
-        const int r0 = w.m0 + t * kRows;
+        const int r0 = t ? w.r1 : w.r0;
         const int kend = r0 >= w.q_len ? 0 : a.causal ? min(w.k_len, r0 + kRows) : w.k_len;
         nbx[t] = (kend + kRows - 1) / kRows;
     }
@@ -565,7 +583,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int ntile = w.nb1 > 0 ? 2 : 1;
                 mbar_expect_tx(&bars.q_full, (uint32_t)(ntile * kTile));
                 for (int t = 0; t < ntile; ++t)
-                    tma_tile(base + t * kTile, &tq, w.hq, w.q0 + w.m0 + t * kRows, &bars.q_full);
+                    tma_tile(base + t * kTile, &tq, t ? w.h1 : w.h0, w.q0 + (t ? w.r1 : w.r0),
+                             &bars.q_full);
                 ++nq;
                 for (int j = 0; j < w.nblk; ++j, ++g) {
                     const int s = (int)(g & 1);
@@ -681,14 +700,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (it < 0) break;
             const Item w = decode_item(a, it, ny);
             const int nbt = t ? w.nb1 : w.nb0;
-            const int qi = w.m0 + t * kRows + r;  // query row within the sequence
+            const int trow = t ? w.r1 : w.r0;  // this tile's first query row and head
+            const int thead = t ? w.h1 : w.h0;
+            const int qi = trow + r;  // query row within the sequence
             const uint32_t base0 = tb0, base1 = tb1;  // blocks of each tile before this item
             tb0 += (uint32_t)w.nb0;
             tb1 += (uint32_t)w.nb1;
             if (nbt == 0) {
                 if (qi < w.q_len) {  // no keys: 0 / 0, as the reference's acc / l
                     T* out = reinterpret_cast<T*>(
-                        a.out + ((int64_t)(w.q0 + qi) * a.ot + (int64_t)w.hq * a.oh) * ES);
+                        a.out + ((int64_t)(w.q0 + qi) * a.ot + (int64_t)thead * a.oh) * ES);
                     for (int d = 0; d < 128; ++d) out[d] = Dt<T>::from_f(__int_as_float(0x7fc00000));
                 }
                 continue;
@@ -704,7 +725,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int kb = j * kRows;
                 // masking only on the blocks that reach past the sequence or the diagonal
                 const bool edge =
-                    kb + kRows > w.k_len || (a.causal && kb + kRows - 1 > w.m0 + t * kRows);
+                    kb + kRows > w.k_len || (a.causal && kb + kRows - 1 > trow);
                 const int lim = klim - kb;  // columns [lim, 128) are masked
                 // the block before's P V is done (S_j was issued after it)
                 if (__any_sync(0xffffffffu, pend != 1.f)) scale_o(sO, pend);
@@ -737,7 +758,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (__any_sync(0xffffffffu, redo)) {
                     const RowState st = redo_rows<T>(
                         reinterpret_cast<const T*>(
-                            a.q + ((int64_t)(w.q0 + qi) * a.qt + (int64_t)w.hq * a.qh) * ES),
+                            a.q + ((int64_t)(w.q0 + qi) * a.qt + (int64_t)thead * a.qh) * ES),
                         a.k + ((int64_t)(w.k0 + kb) * a.kt + (int64_t)w.hk * a.kh) * ES,
                         a.kt * ES, lim, redo, sS, sO, sl2, RowState{m, l});
                     m = st.m;
@@ -768,7 +789,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // segments per store instruction
             const float inv = pend / l;  // a rescale the last block left
             char* stage = base + 6 * kTile + warp * kStage;
-            const int row0 = w.m0 + t * kRows + (warp & 3) * 32;  // the warp's first row
+            const int row0 = trow + (warp & 3) * 32;  // the warp's first row
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 tmem_ld32(sO + 64 * h, sr);
@@ -791,7 +812,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 128 + ((c ^ (rr & 7)) * 16));
                     if (write && row0 + rr < w.q_len) {
                         T* dst = reinterpret_cast<T*>(
-                            a.out + ((int64_t)(w.q0 + row0 + rr) * a.ot + (int64_t)w.hq * a.oh) * ES);
+                            a.out + ((int64_t)(w.q0 + row0 + rr) * a.ot + (int64_t)thead * a.oh) * ES);
                         *reinterpret_cast<uint4*>(dst + 64 * h + 8 * c) = v;
                     }
                 }
@@ -868,10 +889,12 @@ int launch_tc(const VarlenDev& a, int max_q, cudaStream_t stream) {
         !make_map(&tk, a.k, bf, a.Hkv, a.total_k, a.kh, a.kt) ||
         !make_map(&tv, a.v, bf, a.Hkv, a.total_k, a.vh, a.vt))
         return QF_ERR_UNSUPPORTED;
-    // items: (batch x query heads) x 256-query tile rows; every CTA claims
-    // one past the last, so the counter reaches total + grid
-    const int64_t ny = ceil_div(max_q, 2 * kRows);
-    const int64_t total = (int64_t)a.batch * a.Hq * ny;
+    // items: (batch x query heads, or head pairs) x tile rows (128 queries for
+    // head pairs, else 256); every CTA claims one past the last, so the
+    // counter reaches total + grid
+    const bool pair = a.Hkv > 0 && ((a.Hq / a.Hkv) & 1) == 0;  // as head_pairs()
+    const int64_t ny = ceil_div(max_q, pair ? kRows : 2 * kRows);
+    const int64_t total = (int64_t)a.batch * (pair ? a.Hq / 2 : a.Hq) * ny;
     const int64_t sms = sm_count();
     if (total + sms >= ((int64_t)1 << 31)) return QF_ERR_UNSUPPORTED;
     if (total == 0) return QF_OK;
