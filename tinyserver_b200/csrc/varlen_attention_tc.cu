@@ -162,6 +162,24 @@ __device__ __forceinline__ void tma_tile(char* tile, const CUtensorMap* map, int
     tma_load(tile + kSlab, map, 64, head, token, bar);
 }
 
+// TMA store of a {64 elements, 1 head, 32 tokens} box from `src` (128-byte
+// swizzled, as the map says) at (x, head, token); one bulk group per call.
+__device__ __forceinline__ void tma_store(const CUtensorMap* map, int x, int head, int token,
+                                          const void* src) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];\n\t"
+        "cp.async.bulk.commit_group;" ::"l"(reinterpret_cast<uint64_t>(map)),
+        "r"(x), "r"(head), "r"(token), "r"(smem_u32(src))
+        : "memory");
+}
+// This thread's bulk stores have read their shared memory / are complete.
+__device__ __forceinline__ void tma_store_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void tma_store_wait_all() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 #define QF_TMEM_REGS32(r)                                                                       \
     "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),         \
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), \
@@ -505,7 +523,8 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     varlen_attn_tc_kernel(const VarlenDev a, const __grid_constant__ CUtensorMap tq,
                           const __grid_constant__ CUtensorMap tk,
-                          const __grid_constant__ CUtensorMap tv, int ny, int total,
+                          const __grid_constant__ CUtensorMap tv,
+                          const __grid_constant__ CUtensorMap to, int ny, int total,
                           int* work) {
     using P = Packed<T>;
     extern __shared__ __align__(1024) char dsm[];
@@ -784,16 +803,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             ++nit;
             tc_fence_after();
             // O / l, 64 columns at a time: each thread packs its row into the
-            // warp's staging buffer (16-byte chunk c of row r at chunk c ^ r % 8,
-            // no bank conflicts), then the warp writes 4 whole 128-byte row
-            // segments per store instruction
+            // warp's staging buffer (16-byte chunk c of row r at chunk c ^ r % 8:
+            // no bank conflicts, and the 128-byte swizzle a TMA box reads).  A
+            // warp whose 32 rows all lie in the sequence hands the box to a TMA
+            // store (lane 0) and goes on; at the sequence's end the warp writes
+            // its rows itself, 4 whole 128-byte row segments per instruction.
             const float inv = pend / l;  // a rescale the last block left
             char* stage = base + 6 * kTile + warp * kStage;
             const int row0 = trow + (warp & 3) * 32;  // the warp's first row
+            const bool write = !*abort;
+            const bool whole = write && row0 + 32 <= w.q_len;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 tmem_ld32(sO + 64 * h, sr);
                 tmem_ld32(sO + 64 * h + 32, sr + 32);
+                if (lane == 0) tma_store_wait_read();  // the buffer's last store has read it
+                __syncwarp();
                 tmem_wait_ld();
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
@@ -804,16 +829,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                     v.w = P::pack(__uint_as_float(sr[8 * c + 6]) * inv, __uint_as_float(sr[8 * c + 7]) * inv);
                     *reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) * 16)) = v;
                 }
-                __syncwarp();
-                const bool write = !*abort;
+                if (whole) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) tma_store(&to, 64 * h, thead, w.q0 + row0, stage);
+                } else {
+                    __syncwarp();
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int rr = 4 * i + (lane >> 3), c = lane & 7;
-                    const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 128 + ((c ^ (rr & 7)) * 16));
-                    if (write && row0 + rr < w.q_len) {
-                        T* dst = reinterpret_cast<T*>(
-                            a.out + ((int64_t)(w.q0 + row0 + rr) * a.ot + (int64_t)thead * a.oh) * ES);
-                        *reinterpret_cast<uint4*>(dst + 64 * h + 8 * c) = v;
+                    for (int i = 0; i < 8; ++i) {
+                        const int rr = 4 * i + (lane >> 3), c = lane & 7;
+                        const uint4 v =
+                            *reinterpret_cast<const uint4*>(stage + rr * 128 + ((c ^ (rr & 7)) * 16));
+                        if (write && row0 + rr < w.q_len) {
+                            T* dst = reinterpret_cast<T*>(
+                                a.out + ((int64_t)(w.q0 + row0 + rr) * a.ot + (int64_t)thead * a.oh) * ES);
+                            *reinterpret_cast<uint4*>(dst + 64 * h + 8 * c) = v;
+                        }
                     }
                 }
                 __syncwarp();
@@ -823,6 +854,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
+    if (warp < 8 && lane == 0) tma_store_wait_all();  // output stores complete
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
@@ -860,12 +892,12 @@ PFN_cuTensorMapEncodeTiled encode_fn() {
 
 // A 3-D map over (head_dim = 128, heads, tokens) with 64 x 1 x 128 boxes.
 bool make_map(CUtensorMap* map, const char* ptr, int bf16, int64_t heads, int64_t tokens,
-              int64_t head_stride, int64_t token_stride) {
+              int64_t head_stride, int64_t token_stride, int rows = kRows) {
     PFN_cuTensorMapEncodeTiled fn = encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[3] = {128, (cuuint64_t)heads, (cuuint64_t)tokens};
     const cuuint64_t strides[2] = {(cuuint64_t)head_stride * 2, (cuuint64_t)token_stride * 2};
-    const cuuint32_t box[3] = {64, 1, (cuuint32_t)kRows};
+    const cuuint32_t box[3] = {64, 1, (cuuint32_t)rows};
     const cuuint32_t estride[3] = {1, 1, 1};
     return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
               const_cast<char*>(ptr), dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -884,10 +916,11 @@ int launch_tc(const VarlenDev& a, int max_q, cudaStream_t stream) {
         configured.store(true, std::memory_order_relaxed);
     }
     const int bf = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
-    CUtensorMap tq, tk, tv;
+    CUtensorMap tq, tk, tv, to;
     if (!make_map(&tq, a.q, bf, a.Hq, a.total_q, a.qh, a.qt) ||
         !make_map(&tk, a.k, bf, a.Hkv, a.total_k, a.kh, a.kt) ||
-        !make_map(&tv, a.v, bf, a.Hkv, a.total_k, a.vh, a.vt))
+        !make_map(&tv, a.v, bf, a.Hkv, a.total_k, a.vh, a.vt) ||
+        !make_map(&to, a.out, bf, a.Hq, a.total_q, a.oh, a.ot, 32))
         return QF_ERR_UNSUPPORTED;
     // items: (batch x query heads, or head pairs) x tile rows (128 queries for
     // head pairs, else 256); every CTA claims one past the last, so the
@@ -899,7 +932,7 @@ int launch_tc(const VarlenDev& a, int max_q, cudaStream_t stream) {
     if (total + sms >= ((int64_t)1 << 31)) return QF_ERR_UNSUPPORTED;
     if (total == 0) return QF_OK;
     const int64_t grid = a.work_counter ? std::min<int64_t>(total, sms) : total;
-    kernel<<<(unsigned)grid, kThreads, kSmem, stream>>>(a, tq, tk, tv, (int)ny, (int)total,
+    kernel<<<(unsigned)grid, kThreads, kSmem, stream>>>(a, tq, tk, tv, to, (int)ny, (int)total,
                                                          a.work_counter);
     return check_launch();
 }
