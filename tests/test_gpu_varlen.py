@@ -271,3 +271,38 @@ def test_empty_sequences_keyless_rows_and_many_short(causal):
     tsb.check_errors()
     assert_close(out, expected, f"600 short causal={causal}", min_exact=0.0)
     _as_accurate_as_reference(out, q, k, v, cu, cu, causal, f"600 short causal={causal}")
+
+
+def test_benchmark_batch_against_fp32_attention():
+    """The benchmark's own c2 batch (16 sequences, 14,611 tokens, Qwen3-1.7B
+    heads) through the tensor-core path, checked sequence by sequence against
+    plain PyTorch attention in fp32 on the GPU (GQA heads expanded, causal):
+    every element within the bf16 contract, and the mean error small."""
+    import torch.nn.functional as F
+
+    from tinyserver_b200 import workloads as W
+
+    cfg = W.CONFIGS["c2"]
+    s = cfg.shape
+    lens = [n for n, _ in W.sequences(cfg, 0)]
+    T, Hq, Hkv, D = sum(lens), s.num_q_heads, s.num_kv_heads, s.head_dim
+    g = torch.Generator(device=DEV).manual_seed(W.seed_of(cfg, 0) + 9)
+    q = torch.randn(T, Hq, D, generator=g, device=DEV).to(cfg.dtype)
+    k = torch.randn(T, Hkv, D, generator=g, device=DEV).to(cfg.dtype)
+    v = torch.randn(T, Hkv, D, generator=g, device=DEV).to(cfg.dtype)
+    cu = torch.zeros(len(lens) + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(torch.tensor(lens), 0)
+    out = tsb.flash_attn_varlen_func(q, k, v, cu.to(DEV), cu.to(DEV), max(lens), max(lens),
+                                     True)
+    tsb.check_errors()
+    expected = torch.empty_like(out)
+    for b in range(len(lens)):
+        a0, a1 = int(cu[b]), int(cu[b + 1])
+        qs = q[a0:a1].float().transpose(0, 1)[None]
+        ks = k[a0:a1].float().transpose(0, 1).repeat_interleave(Hq // Hkv, 0)[None]
+        vs = v[a0:a1].float().transpose(0, 1).repeat_interleave(Hq // Hkv, 0)[None]
+        o = F.scaled_dot_product_attention(qs, ks, vs, is_causal=True)
+        expected[a0:a1] = o[0].transpose(0, 1).to(cfg.dtype)
+    assert_close(out, expected, "c2 batch vs fp32 attention", min_exact=0.0)
+    err = (out.float() - expected.float()).abs().mean().item()
+    assert err < 2e-3, f"mean abs error {err:.3e}"
