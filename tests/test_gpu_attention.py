@@ -138,3 +138,37 @@ def test_workspace_too_small_is_rejected():
     assert tsb.paged_attention_workspace_bytes(1, 8, 128, 1300) == 1 * 8 * 6 * 130 * 4
     assert tsb.paged_attention_workspace_bytes(1, 8, 128, 256) == 0  # nothing to split
     assert tsb.paged_attention_workspace_bytes(512, 32, 128, 8192) == 512 * 32 * 4 * 130 * 4
+
+
+def test_benchmark_step_against_fp32_attention():
+    """The benchmark's own c3 decode step (256 sequences, 1.04 M context
+    tokens, Qwen3-8B heads, 16-token pages in a 32768-block cache) against
+    plain PyTorch attention in fp32 on the GPU over K/V gathered from each
+    sequence's pages: the bf16 contract, >= 95% of elements bit-exact."""
+    import torch.nn.functional as F
+
+    from tinyserver_b200 import workloads as W
+
+    cfg = W.CONFIGS["c3"]
+    s = cfg.shape
+    b = W.index_data(cfg, shard=0)
+    lens = (b.positions + 1).to(torch.int32)
+    S, Hq, Hkv, D, B = len(b.seqs), s.num_q_heads, s.num_kv_heads, s.head_dim, cfg.block_size
+    g = torch.Generator(device=DEV).manual_seed(W.seed_of(cfg, 0) + 5)
+    pool = torch.randn(2, cfg.num_blocks, Hkv, B, D, generator=g, device=DEV,
+                       dtype=torch.float32).to(cfg.dtype)
+    q = torch.randn(S, Hq, D, generator=g, device=DEV, dtype=torch.float32).to(cfg.dtype)
+    bt = b.block_tables.to(DEV)
+    out = tsb.paged_attention_forward(q, pool[0], pool[1], bt, B, lens.to(DEV))
+    tsb.check_errors()
+    expected = torch.empty_like(out)
+    for i in range(S):
+        L = int(lens[i])
+        blocks = bt[i, :(L + B - 1) // B].long()
+        kk = pool[0][blocks].permute(1, 0, 2, 3).reshape(Hkv, -1, D)[:, :L].float()
+        vv = pool[1][blocks].permute(1, 0, 2, 3).reshape(Hkv, -1, D)[:, :L].float()
+        kk = kk.repeat_interleave(Hq // Hkv, 0)[None]
+        vv = vv.repeat_interleave(Hq // Hkv, 0)[None]
+        o = F.scaled_dot_product_attention(q[i].float()[None, :, None, :], kk, vv)
+        expected[i] = o[0, :, 0, :].to(cfg.dtype)
+    _check(out, expected, "c3 decode step vs fp32 attention", min_exact=0.95)
