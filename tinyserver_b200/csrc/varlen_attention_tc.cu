@@ -293,41 +293,17 @@ __device__ __forceinline__ void mask_quarter(uint32_t* sr, int c0, int lim) {
         if (c0 + e >= lim) sr[e] = __float_as_uint(-INFINITY);
 }
 
-// The row max of S (raw scores, masked), S read in 32-column quarters with the
-// next quarter in flight, four independent three-input max chains.
-__device__ __forceinline__ float row_max(uint32_t sS, bool edge, int lim, uint32_t* sr) {
-    float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
-    tmem_ld32(sS, sr);
-    tmem_wait_ld();
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        uint32_t nx[32];
-        if (q < 3) tmem_ld32(sS + 32 * (q + 1), nx);
-        if (edge) mask_quarter(sr, 32 * q, lim);
-#pragma unroll
-        for (int e = 0; e < 32; e += 8) {
-            mx0 = max3(mx0, __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]));
-            mx1 = max3(mx1, __uint_as_float(sr[e + 2]), __uint_as_float(sr[e + 3]));
-            mx2 = max3(mx2, __uint_as_float(sr[e + 4]), __uint_as_float(sr[e + 5]));
-            mx3 = max3(mx3, __uint_as_float(sr[e + 6]), __uint_as_float(sr[e + 7]));
-        }
-        if (q < 3) {
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) sr[e] = nx[e];
-        }
-    }
-    return max3(mx0, mx1, fmaxf(mx2, mx3));
-}
-
 // p = 2^(s * sl2 - mref) for the 128 columns of S, rounded to T and packed in
 // pairs, quarter by quarter; each quarter's P goes over S columns
 // [16q, 16q + 16), read already and below the quarter in flight.  Returns
 // the row sum of p (two packed accumulator pairs), and in *mx the row max of
-// the raw scores (four three-input max chains).
+// the raw scores (four three-input max chains).  A row with no reference max
+// yet (mref = -inf: its first block) takes the max of the block's first
+// quarter, which the max chains hold once that quarter is in; the reference
+// used comes back in *mused.
 template <typename T>
 __device__ __forceinline__ float p_pass(uint32_t sS, float sl2, float mref, bool edge, int lim,
-                                        uint32_t* sr, float* mx) {
+                                        uint32_t* sr, float* mx, float* mused) {
     using P = Packed<T>;
     float ps0 = 0.f, ps1 = 0.f, ps2 = 0.f, ps3 = 0.f;
     float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
@@ -345,6 +321,10 @@ __device__ __forceinline__ float p_pass(uint32_t sS, float sl2, float mref, bool
             mx1 = max3(mx1, __uint_as_float(sr[e + 2]), __uint_as_float(sr[e + 3]));
             mx2 = max3(mx2, __uint_as_float(sr[e + 4]), __uint_as_float(sr[e + 5]));
             mx3 = max3(mx3, __uint_as_float(sr[e + 6]), __uint_as_float(sr[e + 7]));
+        }
+        if (q == 0 && mref == -INFINITY) {  // (no valid key in the quarter: 0, every p 0)
+            const float q0 = max3(mx0, mx1, fmaxf(mx2, mx3));
+            mref = q0 == -INFINITY ? 0.f : q0 * sl2;
         }
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
@@ -365,6 +345,7 @@ __device__ __forceinline__ float p_pass(uint32_t sS, float sl2, float mref, bool
         }
     }
     *mx = max3(mx0, mx1, fmaxf(mx2, mx3));
+    *mused = mref;
     return (ps0 + ps1) + (ps2 + ps3);
 }
 
@@ -749,31 +730,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // the block before's P V is done (S_j was issued after it)
                 if (__any_sync(0xffffffffu, pend != 1.f)) scale_o(sO, pend);
                 pend = 1.f;
-                // A row's first block takes its max first (sl2 > 0: the launcher
-                // sends other scales to the mma.sync kernel).  Later blocks take
-                // one pass: P against the reference max so far, the block max on
-                // the side.  The reference max moves when the row max has grown
-                // by more than 2^8 (O / l is the same either way): l at once, O
-                // at the next block's start (or in 1 / l after the last), when
-                // this block's P V is done.  Growth beyond 2^kRedoLog2 (p
-                // possibly infinite) redoes the row.
-                const bool first = __any_sync(0xffffffffu, m == -INFINITY);
-                float corr = 1.f;
-                if (first) {
-                    const float mx = row_max(sS, edge, lim, sr) * sl2;
-                    if (mx > m + 8.f) {
-                        corr = m == -INFINITY ? 0.f : ex2(m - mx);
-                        m = mx;
-                    }
-                    const bool grow = j > 0 && corr != 1.f;
-                    if (__any_sync(0xffffffffu, grow)) scale_o(sO, grow ? corr : 1.f);
-                }
-                const float mref = m == -INFINITY ? 0.f : m;  // no key yet: every p is 0
-                float mx;
-                const float ps = p_pass<T>(sS, sl2, mref, edge, lim, sr, &mx);
+                // One pass per block (sl2 > 0: the launcher sends other scales to
+                // the mma.sync kernel): P against the row's reference max m, the
+                // block max on the side; a row's first block takes the max of its
+                // first quarter as m.  m moves when the row max has grown by more
+                // than 2^8 (O / l is the same either way): l at once, O at the next
+                // block's start (or in 1 / l after the last), when this block's
+                // P V is done.  Growth beyond 2^kRedoLog2 (p possibly infinite)
+                // redoes the row.
+                float mx, mu;
+                const float ps = p_pass<T>(sS, sl2, m, edge, lim, sr, &mx, &mu);
                 mx *= sl2;
+                if (m == -INFINITY && mx > -INFINITY) m = mu;  // the first reference
                 // (rows past the sequence, whose O is never stored, are left as they are)
-                const bool redo = !first && qi < w.q_len && mx > m + kRedoLog2;
+                const bool redo = m > -INFINITY && qi < w.q_len && mx > m + kRedoLog2;
                 if (__any_sync(0xffffffffu, redo)) {
                     const RowState st = redo_rows<T>(
                         reinterpret_cast<const T*>(
@@ -783,11 +753,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     m = st.m;
                     l = st.l;
                 }
-                if (first) {
-                    l = l * corr + ps;
-                } else if (!redo) {
+                if (!redo) {
                     if (mx > m + 8.f) {
-                        corr = ex2(m - mx);
+                        const float corr = ex2(m - mx);
                         l = (l + ps) * corr;
                         pend = corr;
                         m = mx;
