@@ -552,6 +552,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
+    // Launched with programmatic dependent launch: the set-up above (shared
+    // memory, tensor memory, parameters only) overlaps the previous kernel's
+    // tail; every global memory access -- the inputs, cu_seqlens, the work
+    // counter -- comes after the previous grid has completed.
+    pdl_wait();
+    pdl_trigger();
 
     if (warp == kTmaWarp) {
         if (lane == 0) {
@@ -900,9 +906,8 @@ int launch_tc(const VarlenDev& a, int max_q, cudaStream_t stream) {
     if (total + sms >= ((int64_t)1 << 31)) return QF_ERR_UNSUPPORTED;
     if (total == 0) return QF_OK;
     const int64_t grid = a.work_counter ? std::min<int64_t>(total, sms) : total;
-    kernel<<<(unsigned)grid, kThreads, kSmem, stream>>>(a, tq, tk, tv, to, (int)ny, (int)total,
-                                                         a.work_counter);
-    return check_launch();
+    return launch_pdl(kernel, (unsigned)grid, (unsigned)kThreads, (size_t)kSmem, stream, a, tq, tk,
+                      tv, to, (int)ny, (int)total, a.work_counter);
 }
 
 }  // namespace
