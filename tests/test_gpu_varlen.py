@@ -306,3 +306,29 @@ def test_benchmark_batch_against_fp32_attention():
     assert_close(out, expected, "c2 batch vs fp32 attention", min_exact=0.0)
     err = (out.float() - expected.float()).abs().mean().item()
     assert err < 2e-3, f"mean abs error {err:.3e}"
+
+
+def test_concurrent_streams_use_separate_work_counters():
+    """Calls on two streams may run at the same time on the GPU; each stream
+    gets its own work counter, so both results match single-stream calls bit
+    for bit."""
+    lens = [900, 1500, 300]
+    ins = []
+    for seed in (150, 151):
+        q, k, v, cu = _packed(lens, 16, 8, 128, torch.bfloat16, seed=seed)
+        ins.append((q.to(DEV), k.to(DEV), v.to(DEV), cu.to(DEV)))
+    ref = [tsb.flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), True)
+           for q, k, v, cu in ins]
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    outs = [None, None]
+    for rep in range(3):
+        for i, st in enumerate(streams):
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(st):
+                q, k, v, cu = ins[i]
+                outs[i] = tsb.flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), True)
+        torch.cuda.synchronize()
+        tsb.check_errors()
+        for i in range(2):
+            assert torch.equal(outs[i], ref[i]), f"stream {i}, repetition {rep}"
