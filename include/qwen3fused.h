@@ -217,7 +217,10 @@ int qf_build_slot_mapping(const int32_t* cu_seqlens, int64_t num_seqs,
  * pass at least qf_paged_attention_workspace_bytes(...) bytes for the
  * longest sequence the block tables allow (max_blocks_per_seq * block_size),
  * or NULL to run one CTA per (sequence, kv head).  A block index outside the
- * cache is skipped and sets QF_FLAG_BAD_BLOCK. */
+ * cache is skipped and sets QF_FLAG_BAD_BLOCK; a seq_lens[s] longer than
+ * max_blocks_per_seq * block_size is cut to that length and sets
+ * QF_FLAG_BAD_TABLE.  max_blocks_per_seq * block_size must stay below 2^31
+ * (QF_ERR_UNSUPPORTED otherwise). */
 typedef struct {
     const void* q; int64_t q_stride_seq, q_stride_head;
     const void* k_cache; const void* v_cache; int64_t cache_strides[4];

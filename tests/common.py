@@ -83,12 +83,27 @@ def expected_pool(before: torch.Tensor, written: list, rows: torch.Tensor) -> to
     return out
 
 
-def untouched_checksum(pool: torch.Tensor, block_mapping: torch.Tensor,
-                       slot_mapping: torch.Tensor) -> int:
-    """Exact integer checksum of every (2, 1, N, Hkv, B, D) pool element outside
-    the rows at (block_mapping[t], :, slot_mapping[t]) -- cheap enough for
-    multi-GB caches (no copy of the pool)."""
+def snapshot_pool(pool: torch.Tensor) -> torch.Tensor:
+    """A copy of a (2, L, N, Hkv, B, D) pool to check unwritten slots against
+    (same device; a c5-sized 26 GB pool fits beside its copy on a B200)."""
+    return pool.clone()
+
+
+def assert_untouched(pool: torch.Tensor, snapshot: torch.Tensor, block_mapping: torch.Tensor,
+                     slot_mapping: torch.Tensor, layer: int = 0, chunk_blocks: int = 8192) -> None:
+    """Every pool element outside the rows (block_mapping[t], :, slot_mapping[t])
+    of ``layer`` equals ``snapshot`` bit for bit (compared as integers, so NaN
+    poison compares too).  ``snapshot`` is consumed: the written rows are
+    copied into it from the pool (their contents are checked elsewhere), then
+    the two are compared chunk by chunk along the block dimension."""
+    snapshot[:, layer, block_mapping, :, slot_mapping, :] = \
+        pool[:, layer, block_mapping, :, slot_mapping, :]
     as_int = {2: torch.int16, 4: torch.int32, 1: torch.int8, 8: torch.int64}[pool.element_size()]
-    total = pool.view(as_int).sum(dtype=torch.int64)
-    rows = pool[:, 0, block_mapping, :, slot_mapping, :].view(as_int).sum(dtype=torch.int64)
-    return int((total - rows).item())
+    n = pool.shape[2]
+    for b0 in range(0, n, chunk_blocks):
+        a = pool[:, :, b0:b0 + chunk_blocks].contiguous().view(as_int)
+        e = snapshot[:, :, b0:b0 + chunk_blocks].contiguous().view(as_int)
+        if not torch.equal(a, e):
+            diff = (a != e).nonzero()[0].tolist()
+            diff[2] += b0
+            raise AssertionError(f"an unwritten cache element changed, first at pool index {diff}")

@@ -127,6 +127,29 @@ def test_block_outside_the_cache_is_flagged_not_read():
         tsb.check_errors()
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("split", [True, False])
+def test_length_beyond_the_block_table_is_cut_and_flagged(dtype, split):
+    """A seq_len longer than its block-table row can describe is cut to the
+    row (no read past the row, no partial past the workspace) and flagged;
+    the output equals a call with the cut length."""
+    lens = [40, 700, 90]
+    q, kc, vc, bt, sl = _paged_inputs(lens, 8, 2, 128, 16, dtype, seed=12)
+    cap = bt.shape[1] * 16
+    long = sl.clone()
+    long[1] = cap + 3000  # far past the row: would need more partitions than the workspace has
+    cut = torch.minimum(long, torch.tensor(cap, dtype=torch.int32))
+    args = (q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), 16)
+    tsb.check_errors()
+    out = tsb.paged_attention_forward(*args, long.to(DEV), split=split)
+    with pytest.raises(IndexError, match="beyond the block table"):
+        tsb.check_errors()
+    expected = tsb.paged_attention_forward(*args, cut.to(DEV), split=split)
+    tsb.check_errors()
+    assert torch.equal(out, expected)
+    _check(out, oracle.paged_attention_decode(q, kc, vc, bt, 16, cut), "cut length")
+
+
 def test_workspace_too_small_is_rejected():
     q, kc, vc, bt, sl = _paged_inputs([1300], 8, 2, 128, 16, torch.bfloat16, seed=5)
     ws = torch.empty(4, dtype=torch.float32, device=DEV)

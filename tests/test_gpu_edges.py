@@ -238,3 +238,32 @@ def test_build_slot_mapping_flags_positions_past_the_table():
     assert bm.tolist() == [5, 6, -1] and sm.tolist() == [0, 1, 0]
     with pytest.raises(IndexError, match="block table"):
         tsb.check_errors()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs on one box")
+def test_ops_on_a_device_that_is_not_current():
+    """Tensors on cuda:1 while cuda:0 is current: every op launches on the
+    tensors' device (and the default stream of that device), not the current
+    one, and leaves the current device as it was."""
+    torch.cuda.set_device(0)
+    d1 = torch.device("cuda", 1)
+    g = torch.Generator(device=d1).manual_seed(5)
+    x = torch.randn(64, 256, generator=g, device=d1).to(torch.bfloat16)
+    w = torch.randn(256, generator=g, device=d1).to(torch.bfloat16)
+    y = tsb.rms_norm(x, w, 1e-6)
+    gu = torch.randn(64, 512, generator=g, device=d1).to(torch.bfloat16)
+    act = tsb.silu_and_mul(gu)
+    tsb.check_errors(d1)
+    assert torch.cuda.current_device() == 0
+    assert_close(y, oracle.rmsnorm(x.cpu(), w.cpu(), 1e-6), "rms_norm on cuda:1")
+    assert_close(act, oracle.silu_and_mul(gu[:, :256].cpu(), gu[:, 256:].cpu()), "silu on cuda:1")
+    lens = torch.tensor([37, 300], dtype=torch.int32)
+    q = torch.randn(2, 8, 128, generator=g, device=d1).to(torch.bfloat16)
+    kc = torch.randn(24, 2, 16, 128, generator=g, device=d1).to(torch.bfloat16)
+    vc = torch.randn(24, 2, 16, 128, generator=g, device=d1).to(torch.bfloat16)
+    bt = torch.arange(24, dtype=torch.int32, device=d1).view(2, 12)
+    out = tsb.paged_attention_forward(q, kc, vc, bt, 16, lens.to(d1))
+    tsb.check_errors(d1)
+    assert_close(out, oracle.paged_attention_decode(q.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), 16,
+                                                    lens), "decode on cuda:1", min_exact=0.98)
+    assert torch.cuda.current_device() == 0

@@ -12,7 +12,7 @@ import torch
 
 import tinyserver_b200 as tsb
 from oracle import oracle
-from tests.common import assert_close, untouched_checksum
+from tests.common import assert_close, assert_untouched, snapshot_pool
 from tinyserver_b200 import workloads as W
 
 pytestmark = pytest.mark.gpu
@@ -92,7 +92,7 @@ def test_qk_norm_rope_store(batch, cos_mode):
     pool = t["kv_pool"]
     bm, sm = t["block_mapping"], t["slot_mapping"]
     before_rows = pool[:, 0, bm, :, sm, :].clone()
-    untouched_before = untouched_checksum(pool, bm, sm)
+    snap = snapshot_pool(pool)
     kw = dict(positions=t["positions"], inv_freq=t["inv_freq"]) if cos_mode == "computed" else {}
     q_out, k_out = tsb.qk_norm_rope_store(
         q, k, v, t["q_norm"], t["k_norm"], s.eps,
@@ -105,7 +105,8 @@ def test_qk_norm_rope_store(batch, cos_mode):
     rows = pool[:, 0, bm, :, sm, :]  # (T, 2, Hkv, D)
     assert torch.equal(rows[:, 0], k_out), "K pages != rotated K"
     assert torch.equal(rows[:, 1], v), "V pages != V"
-    assert untouched_checksum(pool, bm, sm) == untouched_before, "an unwritten slot changed"
+    assert_untouched(pool, snap, bm, sm)
+    del snap
     pool[:, 0, bm, :, sm, :] = before_rows  # leave the cache as the batch made it
 
 

@@ -12,7 +12,7 @@ import torch
 
 import tinyserver_b200 as tsb
 from oracle import oracle
-from tests.common import assert_close, untouched_checksum
+from tests.common import assert_close, assert_untouched, snapshot_pool
 from tinyserver_b200 import workloads as W
 
 pytestmark = pytest.mark.gpu
@@ -68,12 +68,13 @@ def test_qk_norm_rope_store(batch):
     assert torch.allclose((cos.float() ** 2 + sin.float() ** 2), torch.ones_like(cos.float()),
                           atol=2e-2)
     pool, bm, sm = t["kv_pool"], t["block_mapping"], t["slot_mapping"]
-    before = untouched_checksum(pool, bm, sm)
+    snap = snapshot_pool(pool)
     q_out, k_out = tsb.qk_norm_rope_store(q, k, v, t["q_norm"], t["k_norm"], s.eps, cos, sin,
                                           t["k_cache"], t["v_cache"], bm, sm)
     rows = pool[:, 0, bm, :, sm, :]
     assert torch.equal(rows[:, 0], k_out) and torch.equal(rows[:, 1], v)
-    assert untouched_checksum(pool, bm, sm) == before
+    assert_untouched(pool, snap, bm, sm)
+    del snap
     smp = _sample(batch).cuda()
     rq, rk = oracle.qk_norm_rope_store(q[smp].cpu(), k[smp].cpu(), None, t["q_norm"].cpu(),
                                        t["k_norm"].cpu(), s.eps, cos[smp].cpu(), sin[smp].cpu())

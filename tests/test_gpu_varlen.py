@@ -240,6 +240,35 @@ def test_cuda_graph_replays():
         assert torch.equal(out, eager), f"replay {i}"
 
 
+def test_two_graphs_replay_only_the_second():
+    """Two graphs captured one after the other (torch captures both on one
+    shared capture stream); only the second is replayed.  A work counter made
+    during a capture is zeroed only by that graph, so each capture must get a
+    counter of its own rather than share one whose zero fill lives in the
+    other graph."""
+    lens = [513, 64, 1029]
+    q, k, v, cu = _packed(lens, 16, 8, 128, torch.bfloat16, seed=95)
+    q, k, v, cu = q.to(DEV), k.to(DEV), v.to(DEV), cu.to(DEV)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        tsb.flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), True)  # warm-up
+    torch.cuda.current_stream().wait_stream(s)
+    graphs, outs = [], []
+    for _ in range(2):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            outs.append(tsb.flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), True))
+        graphs.append(g)
+    eager = tsb.flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), True)
+    for i in range(3):
+        graphs[1].replay()
+        torch.cuda.synchronize()
+        tsb.check_errors()
+        assert torch.equal(outs[1], eager), f"second graph, replay {i}"
+    del graphs
+
+
 @pytest.mark.parametrize("causal", [True, False])
 def test_empty_sequences_keyless_rows_and_many_short(causal):
     """Edge cases of the packed layout on the tensor-core path: zero-length

@@ -9,6 +9,7 @@ away (one stream sync per op: for tests and debugging, not for serving).
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 
@@ -61,10 +62,30 @@ def stream_ptr(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+_SAME_DEVICE = contextlib.nullcontext()
+
+
+def on_device(device: torch.device):
+    """Make ``device`` the current CUDA device around a launch.  The library
+    launches on the current device, and a stream handle of 0 (torch's default
+    stream) means the current device's default stream, so tensors on cuda:1
+    while cuda:0 is current need the switch.  No switch when it is current."""
+    idx = device.index
+    if idx is None or idx == torch.cuda.current_device():
+        return _SAME_DEVICE
+    return torch.cuda.device(idx)
+
+
 def status_word(device: torch.device) -> torch.Tensor:
     idx = device.index if device.index is not None else torch.cuda.current_device()
     w = _status_words.get(idx)
     if w is None:
+        if torch.cuda.is_current_stream_capturing():
+            # made here, the word would be zeroed only by a node of this graph
+            # and would live in the graph's private memory pool
+            raise RuntimeError("tinyserver_b200: call any op on this device once outside "
+                               "CUDA graph capture before capturing (it makes the device's "
+                               "status word)")
         w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
         _status_words[idx] = w
     return w
@@ -79,9 +100,15 @@ def work_counter(device: torch.device) -> torch.Tensor:
     idx = device.index if device.index is not None else torch.cuda.current_device()
     key = (idx, stream_ptr(torch.device("cuda", idx)))
     w = _work_counters.get(key)
-    if w is None:
-        w = torch.zeros(2, dtype=torch.int32, device=torch.device("cuda", idx))
-        _work_counters[key] = w
+    if w is not None:
+        return w
+    w = torch.zeros(2, dtype=torch.int32, device=torch.device("cuda", idx))
+    if torch.cuda.is_current_stream_capturing():
+        # Made during a CUDA graph capture, this pair's zero fill exists only as
+        # a node of that graph, so it is not kept for later calls: this call
+        # gets a pair of its own that the graph zeroes on every replay.
+        return w
+    _work_counters[key] = w
     return w
 
 
@@ -93,8 +120,9 @@ def read_flags(device: torch.device, clear: bool = True) -> int:
     """Synchronise the current stream and return (and clear) the status word."""
     w = status_word(device)
     out = ctypes.c_int32(0)
-    rc = _capi.lib().qf_read_status(w.data_ptr(), ctypes.byref(out), int(clear),
-                                    stream_ptr(device))
+    with on_device(device):
+        rc = _capi.lib().qf_read_status(w.data_ptr(), ctypes.byref(out), int(clear),
+                                        stream_ptr(device))
     if rc not in (_capi.QF_OK, _capi.QF_ERR_DEVICE):
         _capi.check(rc, "qf_read_status")
     return out.value

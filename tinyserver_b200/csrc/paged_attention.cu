@@ -20,7 +20,8 @@
 //    partition leaves per-partition (max, sum, acc) in a caller-provided fp32
 //    workspace and a second kernel merges them.
 // Keys past seq_len are never read; a block index outside the cache is
-// skipped and flagged (QF_FLAG_BAD_BLOCK).
+// skipped and flagged (QF_FLAG_BAD_BLOCK); a seq_len longer than its
+// block-table row is cut to the row and flagged (QF_FLAG_BAD_TABLE).
 #include <math.h>
 
 #include "qf_common.cuh"
@@ -69,6 +70,20 @@ struct AttnDev {
     int32_t* status;
 };
 
+// Keys of sequence s that the kernels may read: seq_lens[s], clamped to what
+// its block-table row can describe (max_blocks * B).  A longer length would
+// index past the row and need more partitions than the workspace holds, so it
+// is cut to the row and flagged QF_FLAG_BAD_TABLE (by one thread of each CTA).
+__device__ __forceinline__ int seq_keys(const AttnDev& a, int s) {
+    int L = __ldg(a.lens + s);
+    const int64_t cap = a.max_blocks * a.B;
+    if ((int64_t)L > cap) {
+        if (threadIdx.x == 0) flag(a.status, QF_FLAG_BAD_TABLE);
+        L = (int)cap;
+    }
+    return L;
+}
+
 // Load PER elements of one row (PER * sizeof(T) bytes: 4, 8 or a multiple of
 // 16) as floats.
 template <typename T, int PER>
@@ -95,7 +110,7 @@ __global__ void __launch_bounds__(kAttnThreads) paged_decode_kernel(const AttnDe
     constexpr int NCH = D / EPV;       // 16-byte chunks per row
     constexpr int PER = D / 32;        // output elements per lane in PV
     const int p = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
-    const int L = __ldg(a.lens + s);
+    const int L = seq_keys(a, s);
     const int k_begin = p * a.part;
     if (p > 0 && k_begin >= L) return;  // partition past the sequence (p = 0 always runs)
     const int k_end = min(L, k_begin + a.part);
@@ -252,7 +267,7 @@ __global__ void __launch_bounds__(kAttnThreads) paged_decode_kernel(const AttnDe
 template <typename T, int D>
 __global__ void __launch_bounds__(128) paged_decode_merge_kernel(const AttnDev a) {
     const int hq = blockIdx.x, s = blockIdx.y;
-    const int L = __ldg(a.lens + s);
+    const int L = seq_keys(a, s);
     const int nparts = L > a.part ? (L + a.part - 1) / a.part : 1;
     if (nparts == 1) return;
     const float* w = a.ws + ((int64_t)s * a.Hq + hq) * a.P * (D + 2);
@@ -305,7 +320,7 @@ __global__ void __launch_bounds__(kAttnThreads) paged_decode_mma_kernel(const At
     using P = Packed<T>;
     constexpr int TK = MT::TK, NCH = MT::NCH, NT = D / 8, KS = D / 16;
     const int p = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
-    const int L = __ldg(a.lens + s);
+    const int L = seq_keys(a, s);
     const int k_begin = p * a.part;
     if (p > 0 && k_begin >= L) return;
     const int k_end = min(L, k_begin + a.part);
@@ -588,12 +603,17 @@ extern "C" size_t qf_paged_attention_workspace_bytes(int64_t num_seqs, int64_t n
     if (num_seqs <= 0 || num_q_heads <= 0 || head_dim <= 0 || max_seq_len <= 0) return 0;
     const int64_t P = qf::partitions(max_seq_len, qf::partition_keys(num_seqs, max_seq_len));
     if (P == 1) return 0;
-    return (size_t)(num_seqs * num_q_heads * P * (head_dim + 2) * (int64_t)sizeof(float));
+    int64_t n = 0;  // num_seqs * num_q_heads * P * (head_dim + 2) floats; SIZE_MAX on overflow
+    if (__builtin_mul_overflow(num_seqs, num_q_heads, &n) || __builtin_mul_overflow(n, P, &n) ||
+        __builtin_mul_overflow(n, head_dim + 2, &n) ||
+        __builtin_mul_overflow(n, (int64_t)sizeof(float), &n))
+        return SIZE_MAX;
+    return (size_t)n;
 }
 
-extern "C" int qf_paged_attention_decode(const qf_paged_attention_args* p, cudaStream_t stream) {
-    if (!p) return QF_ERR_INVALID;
-    const qf_paged_attention_args& g = *p;
+namespace {
+// Argument checks shared by both decode entry points, before any device work.
+int check_decode_args(const qf_paged_attention_args& g) {
     if (g.num_seqs < 0 || g.num_q_heads <= 0 || g.num_kv_heads <= 0 || g.block_size <= 0 ||
         g.num_blocks < 0 || g.max_blocks_per_seq < 0)
         return QF_ERR_INVALID;
@@ -602,14 +622,26 @@ extern "C" int qf_paged_attention_decode(const qf_paged_attention_args* p, cudaS
         return QF_ERR_INVALID;
     if (g.num_q_heads % g.num_kv_heads) return QF_ERR_INVALID;
     if (g.num_seqs > 65535 || g.num_kv_heads > 65535) return QF_ERR_UNSUPPORTED;
+    // key indices are int on the device: a block-table row describes < 2^31 keys
+    if (g.max_blocks_per_seq > INT32_MAX / g.block_size) return QF_ERR_UNSUPPORTED;
+    if (g.dtype != QF_F32 && g.dtype != QF_F16 && g.dtype != QF_BF16) return QF_ERR_INVALID;
     const int64_t D = g.head_dim;
     const int64_t es = g.dtype == QF_F32 ? 4 : 2;
-    if (g.dtype != QF_F32 && g.dtype != QF_F16 && g.dtype != QF_BF16) return QF_ERR_INVALID;
     // K rows are read in 16-byte chunks, V row slices in D/32-element pieces
     if ((D * es) % 16 || (g.cache_strides[0] * es) % 16 || (g.cache_strides[1] * es) % 16 ||
         (g.cache_strides[2] * es) % 16 || g.cache_strides[3] != 1 || !qf::aligned16(g.k_cache) ||
         !qf::aligned16(g.v_cache))
         return QF_ERR_UNSUPPORTED;
+    return QF_OK;
+}
+}  // namespace
+
+extern "C" int qf_paged_attention_decode(const qf_paged_attention_args* p, cudaStream_t stream) {
+    if (!p) return QF_ERR_INVALID;
+    const qf_paged_attention_args& g = *p;
+    const int rc = check_decode_args(g);
+    if (rc || g.num_seqs == 0) return rc;
+    const int64_t D = g.head_dim;
     qf::AttnDev a{};
     a.q = static_cast<const char*>(g.q);
     a.qs = g.q_stride_seq;
@@ -703,20 +735,18 @@ extern "C" size_t qf_paged_attention_noalloc_capacity(void) { return kNoAllocScr
 extern "C" int qf_paged_attention_decode_noalloc(const qf_paged_attention_args* p,
                                                  cudaStream_t stream) {
     if (!p) return QF_ERR_INVALID;
+    const int rc0 = check_decode_args(*p);  // an invalid call is refused as such, not as too big
+    if (rc0 || p->num_seqs == 0) return rc0;
+    // check_decode_args bounds max_blocks_per_seq * block_size below 2^31
     const int64_t max_len = std::max<int64_t>(1, p->max_blocks_per_seq * p->block_size);
-    if (p->num_seqs > 0 && p->num_q_heads > 0 && p->head_dim > 0 &&
-        qf_paged_attention_workspace_bytes(p->num_seqs, p->num_q_heads, p->head_dim, max_len) >
-            kNoAllocScratchBytes)
+    if (qf_paged_attention_workspace_bytes(p->num_seqs, p->num_q_heads, p->head_dim, max_len) >
+        kNoAllocScratchBytes)
         return QF_ERR_SCRATCH;  // checked before any device work
     qf_paged_attention_args a = *p;
-    a.workspace = nullptr;
-    a.workspace_bytes = 0;
-    if (a.num_seqs > 0) {
-        void* ptr = nullptr;
-        const int rc = scratch_address(&ptr);
-        if (rc) return rc;
-        a.workspace = ptr;
-        a.workspace_bytes = (int64_t)kNoAllocScratchBytes;
-    }
+    void* ptr = nullptr;
+    const int rc = scratch_address(&ptr);
+    if (rc) return rc;
+    a.workspace = ptr;
+    a.workspace_bytes = (int64_t)kNoAllocScratchBytes;
     return qf_paged_attention_decode(&a, stream);
 }

@@ -585,19 +585,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ++n;
                 if (done) break;
                 if (w.nblk == 0) continue;  // no keys: nothing to load
-                if (nq > 0) mbar_wait(&bars.q_empty, (nq - 1) & 1, abort);
+                // after a wait that gave up, no further copy is issued: the
+                // stage may still be read by the tensor core
+                if (nq > 0 && !mbar_wait(&bars.q_empty, (nq - 1) & 1, abort)) break;
                 const int ntile = w.nb1 > 0 ? 2 : 1;
                 mbar_expect_tx(&bars.q_full, (uint32_t)(ntile * kTile));
                 for (int t = 0; t < ntile; ++t)
                     tma_tile(base + t * kTile, &tq, t ? w.h1 : w.h0, w.q0 + (t ? w.r1 : w.r0),
                              &bars.q_full);
                 ++nq;
+                bool ok = true;
                 for (int j = 0; j < w.nblk; ++j, ++g) {
                     const int s = (int)(g & 1);
-                    if (g >= 2) mbar_wait(&bars.k_empty[s], ((g - 2) >> 1) & 1, abort);
+                    if (g >= 2 && !mbar_wait(&bars.k_empty[s], ((g - 2) >> 1) & 1, abort)) {
+                        ok = false;
+                        break;
+                    }
                     mbar_expect_tx(&bars.k_full[s], (uint32_t)kTile);
                     tma_tile(base + (2 + s) * kTile, &tk, w.hk, w.k0 + j * kRows, &bars.k_full[s]);
                 }
+                if (!ok) break;
             }
             // every copy issued has landed before the CTA can leave
             if (nq > 0) mbar_wait(&bars.q_full, (nq - 1) & 1, nullptr);
@@ -614,12 +621,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ++n;
                 if (it < 0) break;
                 const Item w = decode_item(a, it, ny);
+                bool ok = true;
                 for (int j = 0; j < w.nblk; ++j, ++g) {
                     const int s = (int)(g & 1);
-                    if (g >= 2) mbar_wait(&bars.v_empty[s], ((g - 2) >> 1) & 1, abort);
+                    if (g >= 2 && !mbar_wait(&bars.v_empty[s], ((g - 2) >> 1) & 1, abort)) {
+                        ok = false;  // gave up: issue no further copy
+                        break;
+                    }
                     mbar_expect_tx(&bars.v_full[s], (uint32_t)kTile);
                     tma_tile(base + (4 + s) * kTile, &tv, w.hk, w.k0 + j * kRows, &bars.v_full[s]);
                 }
+                if (!ok) break;
             }
             for (uint32_t d = g > 2 ? g - 2 : 0; d < g; ++d)
                 mbar_wait(&bars.v_full[d & 1], (d >> 1) & 1, nullptr);

@@ -16,7 +16,7 @@ import math
 import torch
 
 from .. import _capi
-from .._runtime import (after_op, dtype_tag, require_cuda, status_word, stream_ptr,
+from .._runtime import (after_op, dtype_tag, on_device, require_cuda, status_word, stream_ptr,
                         work_counter)
 
 __all__ = ["flash_attn_varlen_func", "paged_attention_forward", "paged_attention_workspace_bytes"]
@@ -88,7 +88,8 @@ def paged_attention_forward(query: torch.Tensor, k_cache: torch.Tensor, v_cache:
                 workspace.numel() * workspace.element_size()
     a.dtype = tag
     a.status = status_word(dev).data_ptr()
-    rc = _capi.lib().qf_paged_attention_decode(a, stream_ptr(dev))
+    with on_device(dev):
+        rc = _capi.lib().qf_paged_attention_decode(a, stream_ptr(dev))
     _capi.check(rc, "paged_attention_forward")
     after_op(dev)
     return out
@@ -136,7 +137,8 @@ def flash_attn_varlen_func(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     a.status = status_word(dev).data_ptr()
     a.total_q, a.total_k = Tq, Tk
     a.work_counter = work_counter(dev).data_ptr()
-    rc = _capi.lib().qf_varlen_attention(a, stream_ptr(dev))
+    with on_device(dev):
+        rc = _capi.lib().qf_varlen_attention(a, stream_ptr(dev))
     _capi.check(rc, "flash_attn_varlen_func")
     after_op(dev)
     return out

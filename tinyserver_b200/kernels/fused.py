@@ -22,7 +22,8 @@ import ctypes
 import torch
 
 from .. import _capi
-from .._runtime import after_op, dtype_tag, index_tag, require_cuda, status_word, stream_ptr
+from .._runtime import (after_op, dtype_tag, index_tag, on_device, require_cuda, status_word,
+                        stream_ptr)
 
 __all__ = ["embedding", "rms_norm", "fused_add_rms_norm", "rope_cos_sin", "rope_inv_freq",
            "apply_rotary_pos_emb", "qk_norm_rope_store", "silu_and_mul", "build_slot_mapping"]
@@ -51,9 +52,10 @@ def embedding(input_ids: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     if weight.stride(1) != 1:
         weight = weight.contiguous()
     out = torch.empty(ids.numel(), H, dtype=weight.dtype, device=dev)
-    rc = _capi.lib().qf_embedding(ids.data_ptr(), itag, weight.data_ptr(), V, weight.stride(0),
-                                  out.data_ptr(), H, ids.numel(), H, weight.element_size(),
-                                  status_word(dev).data_ptr(), stream_ptr(dev))
+    with on_device(dev):
+        rc = _capi.lib().qf_embedding(ids.data_ptr(), itag, weight.data_ptr(), V, weight.stride(0),
+                                      out.data_ptr(), H, ids.numel(), H, weight.element_size(),
+                                      status_word(dev).data_ptr(), stream_ptr(dev))
     _capi.check(rc, "embedding")
     after_op(dev)
     return out.view(*input_ids.shape, H)
@@ -75,9 +77,10 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float,
     if y2.data_ptr() != y.data_ptr() and out is not None:
         raise ValueError("rms_norm: out must be viewable as rows")
     w = weight.contiguous()
-    rc = _capi.lib().qf_rmsnorm(x2.data_ptr(), x2.stride(0), w.data_ptr(), y2.data_ptr(),
-                                y2.stride(0), x2.shape[0], x2.shape[1], float(eps), tag,
-                                stream_ptr(dev))
+    with on_device(dev):
+        rc = _capi.lib().qf_rmsnorm(x2.data_ptr(), x2.stride(0), w.data_ptr(), y2.data_ptr(),
+                                    y2.stride(0), x2.shape[0], x2.shape[1], float(eps), tag,
+                                    stream_ptr(dev))
     _capi.check(rc, "rms_norm")
     return y
 
@@ -110,10 +113,11 @@ def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Te
     y = torch.empty(x.shape, dtype=x.dtype, device=dev)
     y2 = y.view(-1, x.shape[-1])
     w = weight.contiguous()
-    rc = _capi.lib().qf_add_rmsnorm(x2.data_ptr(), x2.stride(0), r2.data_ptr(), r2.stride(0),
-                                    w.data_ptr(), h2.data_ptr(), h2.stride(0), y2.data_ptr(),
-                                    y2.stride(0), x2.shape[0], x2.shape[1], float(eps), tag,
-                                    stream_ptr(dev))
+    with on_device(dev):
+        rc = _capi.lib().qf_add_rmsnorm(x2.data_ptr(), x2.stride(0), r2.data_ptr(), r2.stride(0),
+                                        w.data_ptr(), h2.data_ptr(), h2.stride(0), y2.data_ptr(),
+                                        y2.stride(0), x2.shape[0], x2.shape[1], float(eps), tag,
+                                        stream_ptr(dev))
     _capi.check(rc, "fused_add_rms_norm")
     return y, h
 
@@ -145,9 +149,10 @@ def rope_cos_sin(position_ids: torch.Tensor, inv_freq: torch.Tensor, head_dim: i
     inv = inv_freq.to(torch.float32).contiguous()
     cos = torch.empty(*position_ids.shape, head_dim, dtype=dtype, device=dev)
     sin = torch.empty_like(cos)
-    rc = _capi.lib().qf_rope_cos_sin(pos.data_ptr(), itag, inv.data_ptr(), pos.numel(),
-                                     head_dim, float(scaling), _dtype_of(dtype), cos.data_ptr(),
-                                     sin.data_ptr(), stream_ptr(dev))
+    with on_device(dev):
+        rc = _capi.lib().qf_rope_cos_sin(pos.data_ptr(), itag, inv.data_ptr(), pos.numel(),
+                                         head_dim, float(scaling), _dtype_of(dtype), cos.data_ptr(),
+                                         sin.data_ptr(), stream_ptr(dev))
     _capi.check(rc, "rope_cos_sin")
     return cos, sin
 
@@ -257,7 +262,8 @@ def qk_norm_rope_store(
     a.num_tokens, a.num_q_heads, a.num_kv_heads, a.head_dim = T, Hq, Hkv, D
     a.dtype = tag
     a.status = status_word(dev).data_ptr()
-    rc = _capi.lib().qf_qk_norm_rope_store(ctypes.byref(a), stream_ptr(dev))
+    with on_device(dev):
+        rc = _capi.lib().qf_qk_norm_rope_store(ctypes.byref(a), stream_ptr(dev))
     _capi.check(rc, "qk_norm_rope_store")
     after_op(dev)
     return q_out, k_out
@@ -316,9 +322,10 @@ def silu_and_mul(gate: torch.Tensor, up: torch.Tensor | None = None,
     if out is None:
         out = torch.empty(out_shape, dtype=g_rows.dtype, device=dev)
     o2 = out.view(-1, I)
-    rc = _capi.lib().qf_silu_and_mul(g_rows.data_ptr(), g_rows.stride(0), u_rows.data_ptr(),
-                                     u_rows.stride(0), o2.data_ptr(), o2.stride(0),
-                                     g_rows.shape[0], I, tag, stream_ptr(dev))
+    with on_device(dev):
+        rc = _capi.lib().qf_silu_and_mul(g_rows.data_ptr(), g_rows.stride(0), u_rows.data_ptr(),
+                                         u_rows.stride(0), o2.data_ptr(), o2.stride(0),
+                                         g_rows.shape[0], I, tag, stream_ptr(dev))
     _capi.check(rc, "silu_and_mul")
     return out
 
@@ -339,10 +346,11 @@ def build_slot_mapping(cu_seqlens: torch.Tensor, positions: torch.Tensor,
     T = pos.numel()
     bm = torch.empty(T, dtype=torch.int64, device=dev)
     sm = torch.empty(T, dtype=torch.int64, device=dev)
-    rc = _capi.lib().qf_build_slot_mapping(cu.data_ptr(), cu.numel() - 1, pos.data_ptr(), T,
-                                           bt.data_ptr(), bt.stride(0), bt.shape[1],
-                                           int(block_size), bm.data_ptr(), sm.data_ptr(),
-                                           status_word(dev).data_ptr(), stream_ptr(dev))
+    with on_device(dev):
+        rc = _capi.lib().qf_build_slot_mapping(cu.data_ptr(), cu.numel() - 1, pos.data_ptr(), T,
+                                               bt.data_ptr(), bt.stride(0), bt.shape[1],
+                                               int(block_size), bm.data_ptr(), sm.data_ptr(),
+                                               status_word(dev).data_ptr(), stream_ptr(dev))
     _capi.check(rc, "build_slot_mapping")
     after_op(dev)
     return bm, sm

@@ -20,7 +20,7 @@ from __future__ import annotations
 import torch
 
 from .. import _capi
-from .._runtime import after_op, index_tag, require_cuda, status_word, stream_ptr
+from .._runtime import after_op, index_tag, on_device, require_cuda, status_word, stream_ptr
 
 __all__ = ["store_kv_cache", "store_kv_cache_batched"]
 
@@ -78,14 +78,15 @@ def store_kv_cache(
     num_kv_heads, num_tokens, head_dim = k_src.shape
     if block_table.stride(0) != 1 and block_table.numel() > 1:
         block_table = block_table.contiguous()
-    rc = _capi.lib().qf_kv_store_seq(
-        start_position, block_table.data_ptr(), block_table.numel(), itag,
-        k_src.data_ptr(), _capi.i64_array(k_src.stride()),
-        v_src.data_ptr(), _capi.i64_array(v_src.stride()),
-        k_cache.data_ptr(), _capi.i64_array(k_cache.stride()),
-        v_cache.data_ptr(), _capi.i64_array(v_cache.stride()),
-        num_tokens, num_kv_heads, head_dim, k_cache.shape[0], k_cache.shape[2],
-        k_src.element_size(), status_word(dev).data_ptr(), stream_ptr(dev))
+    with on_device(dev):
+        rc = _capi.lib().qf_kv_store_seq(
+            start_position, block_table.data_ptr(), block_table.numel(), itag,
+            k_src.data_ptr(), _capi.i64_array(k_src.stride()),
+            v_src.data_ptr(), _capi.i64_array(v_src.stride()),
+            k_cache.data_ptr(), _capi.i64_array(k_cache.stride()),
+            v_cache.data_ptr(), _capi.i64_array(v_cache.stride()),
+            num_tokens, num_kv_heads, head_dim, k_cache.shape[0], k_cache.shape[2],
+            k_src.element_size(), status_word(dev).data_ptr(), stream_ptr(dev))
     _capi.check(rc, "store_kv_cache")
     after_op(dev)
 
@@ -132,13 +133,14 @@ def store_kv_cache_batched(
                        slot_mapping)
     block_mapping = block_mapping.contiguous()
     slot_mapping = slot_mapping.contiguous()
-    rc = _capi.lib().qf_kv_store_batched(
-        k_src.data_ptr(), _capi.i64_array(k_src.stride()),
-        v_src.data_ptr(), _capi.i64_array(v_src.stride()),
-        k_cache.data_ptr(), _capi.i64_array(k_cache.stride()),
-        v_cache.data_ptr(), _capi.i64_array(v_cache.stride()),
-        block_mapping.data_ptr(), slot_mapping.data_ptr(), itag,
-        num_tokens, num_key_value_heads, head_dim, k_cache.shape[0], k_cache.shape[2],
-        k_src.element_size(), status_word(dev).data_ptr(), stream_ptr(dev))
+    with on_device(dev):
+        rc = _capi.lib().qf_kv_store_batched(
+            k_src.data_ptr(), _capi.i64_array(k_src.stride()),
+            v_src.data_ptr(), _capi.i64_array(v_src.stride()),
+            k_cache.data_ptr(), _capi.i64_array(k_cache.stride()),
+            v_cache.data_ptr(), _capi.i64_array(v_cache.stride()),
+            block_mapping.data_ptr(), slot_mapping.data_ptr(), itag,
+            num_tokens, num_key_value_heads, head_dim, k_cache.shape[0], k_cache.shape[2],
+            k_src.element_size(), status_word(dev).data_ptr(), stream_ptr(dev))
     _capi.check(rc, "store_kv_cache_batched")
     after_op(dev)

@@ -20,7 +20,7 @@ from collections.abc import Sequence
 import torch
 
 from .. import _capi
-from .._runtime import require_cuda, stream_ptr
+from .._runtime import on_device, require_cuda, stream_ptr
 
 __all__ = ["LOWEST_TEMPERATURE", "sample_tokens", "sample_tokens_seeded", "uniforms_from_seeds"]
 
@@ -86,7 +86,8 @@ def _launch(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor
         sd, st = seeds.to(torch.int64).contiguous(), steps.to(torch.int64).contiguous()
         a.seeds, a.steps = sd.data_ptr(), st.data_ptr()
     a.out = out.data_ptr()
-    _capi.check(_capi.lib().qf_sample_tokens(a, stream_ptr(dev)), what)
+    with on_device(dev):
+        _capi.check(_capi.lib().qf_sample_tokens(a, stream_ptr(dev)), what)
     return out
 
 
@@ -133,8 +134,9 @@ def uniforms_from_seeds(seeds: Sequence[int] | torch.Tensor, steps: Sequence[int
     sd, st = _as_u64_bits(seeds, dev), _as_u64_bits(steps, dev)
     require_cuda("uniforms_from_seeds", sd, st)
     out = torch.empty(sd.numel(), dtype=torch.float32, device=dev)
-    rc = _capi.lib().qf_uniforms_from_seeds(sd.contiguous().data_ptr(),
-                                            st.contiguous().data_ptr(), sd.numel(),
-                                            out.data_ptr(), stream_ptr(dev))
+    with on_device(dev):
+        rc = _capi.lib().qf_uniforms_from_seeds(sd.contiguous().data_ptr(),
+                                                st.contiguous().data_ptr(), sd.numel(),
+                                                out.data_ptr(), stream_ptr(dev))
     _capi.check(rc, "uniforms_from_seeds")
     return out
