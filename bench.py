@@ -21,6 +21,18 @@ inputs).  Ranks shard tokens (weak scaling, no collective on the timed path).
 `e2e` runs the same step through the public API from pinned host buffers with
 the H2D copies of every per-step input and the D2H copies of every output
 inside the timed region.
+
+After the timed passes (never inside them):
+  * `validation` -- every 64th token of the global batch: each rank's outputs
+    and the K/V page rows it wrote are all-gathered to rank 0 (NCCL), which
+    regenerates every rank's seeded inputs and checks them against the CPU
+    oracle (the checker, not a measured leg);
+  * `reference_gpu` (N=1) -- the reference's own GPU path on the same batch
+    (its transformers modules on CUDA + its Triton KV store);
+  * `rows` (N=1) -- the other configurations and the next rows of the path,
+    each with its roofline, clocks, end-to-end, CPU baseline and reference-GPU
+    figures: the c3 decode step (eager and CUDA graph), c5 at full size, the
+    standalone KV store, decode and prefill attention and the sampler.
 """
 
 from __future__ import annotations
@@ -41,6 +53,7 @@ sys.path.insert(0, ROOT)
 METRIC = "fused-layer tokens/s and HBM GB/s (% of ~8 TB/s) per B200, Qwen3-8B shapes"
 CONFIG = "c4"
 FALLBACK_HBM_GBS = 6650.0
+VALIDATE_EVERY = 64  # validation samples every 64th token of the global batch
 
 
 # ----------------------------------------------------------------------------
@@ -51,6 +64,15 @@ def hbm_peak() -> tuple[float, str]:
             return float(json.load(f)["hbm_gbs"]), "measured"
     except (OSError, KeyError, ValueError):
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def tensor_peak() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
 
 
 def ncu_traffic(kernel: str) -> float | None:
@@ -116,6 +138,38 @@ class ClockSampler:
                     reasons.add(name)
         return {"sm_mhz": statistics.median(busy), "sm_max_mhz": self.max_mhz,
                 "reasons": sorted(reasons), "samples": len(self.samples)}
+
+
+def timed(fn, steps: int, warmup: int, device_index: int) -> tuple[float, dict]:
+    """Mean ms per call of ``fn`` over ``steps`` back-to-back calls between two
+    CUDA events on the current stream (after ``warmup`` calls), with the SM
+    clocks sampled meanwhile.  A timed region shorter than ~0.2 s is repeated
+    until the clock sampler has seen it."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(device_index).start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    total_ms, n, t_end = 0.0, 0, time.perf_counter() + 0.2
+    while n == 0 or time.perf_counter() < t_end:
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        total_ms += e0.elapsed_time(e1)
+        n += steps
+    return total_ms / n, sampler.stop()
+
+
+def roofline(bound: str, kernel: str, achieved: float, unit: str, traffic=None, **extra) -> dict:
+    peak, kind = hbm_peak() if bound == "hbm" else tensor_peak()
+    src = "hbm_gbs" if bound == "hbm" else "bf16_tflops (cuBLAS burst)"
+    return {"bound": bound, "kernel": kernel, "achieved": round(achieved, 1), "peak": peak,
+            "unit": unit, "frac": round(achieved / peak, 4),
+            "peak_source": f"{kind} {src}" + (" of MEASURED_PEAKS.json" if kind == "measured"
+                                               else " (fallback)"),
+            "traffic": traffic, **extra}
 
 
 # ----------------------------------------------------------------------------
@@ -265,13 +319,174 @@ def measure_e2e(args, step: "Step", t: dict, dev: torch.device, world: int):
 
 
 # ----------------------------------------------------------------------------
+# validation of the outputs (after the timed passes)
+def _within(actual: torch.Tensor, expected: torch.Tensor, exact: bool) -> dict:
+    """The parity contract: bit-exact, or |a - e| <= 2e-2 + 1e-2 |e| (bf16)."""
+    a, e = actual.float(), expected.float()
+    err = (a - e).abs()
+    as_int = {2: torch.int16, 4: torch.int32}[actual.element_size()]
+    same = actual.reshape(-1).view(as_int) == expected.reshape(-1).view(as_int)
+    ok = bool(same.all()) if exact else bool((err <= 2e-2 + 1e-2 * e.abs()).all()) and \
+        bool(torch.isfinite(a).all())
+    return {"ok": ok, "bit_exact": round(float(same.float().mean()), 6),
+            "mismatched": int((~same).sum()),
+            "max_abs_err": float(err.max()) if err.numel() else 0.0}
+
+
+def _expected_rows(t: dict, rows: torch.Tensor, shape, dtype) -> dict:
+    """Oracle outputs of the fused step for the token rows ``rows`` of a
+    batch's tensors ``t`` (inputs sliced on the device, oracle on the CPU)."""
+    from oracle import oracle
+    from tinyserver_b200 import workloads as W
+
+    s = shape
+    cpu = lambda x: x[rows].cpu()  # noqa: E731
+    x0 = t["embed_weight"][t["input_ids"][rows]].cpu()  # the row gather itself
+    y1, h1 = oracle.add_rmsnorm(cpu(t["x_mlp"]), x0, t["input_layernorm"].cpu(), s.eps)
+    q, k, v = W.qkv_views(cpu(t["qkv"]), s)
+    cos, sin = oracle.rope_cos_sin(cpu(t["positions"]), t["inv_freq"].cpu(), s.head_dim, dtype)
+    q_out, k_out = oracle.qk_norm_rope_store(q, k, None, t["q_norm"].cpu(), t["k_norm"].cpu(),
+                                             s.eps, cos, sin)
+    y2, h2 = oracle.add_rmsnorm(cpu(t["attn_out"]), h1, t["post_attention_layernorm"].cpu(),
+                                s.eps)
+    I = s.intermediate
+    gu = cpu(t["gate_up"])
+    act = oracle.silu_and_mul(gu[:, :I], gu[:, I:])
+    return {"normed_in": y1, "q": q_out, "normed_post": y2, "residual": h2, "act": act,
+            "k_page": k_out, "v_page": v}
+
+
+_OUT_ORDER = ["normed_in", "q", "normed_post", "residual", "act", "k_page", "v_page"]
+_EXACT = {"residual", "v_page"}  # one rounding of an add / a copy: bit-exact
+
+
+def _sample_rows(outs: dict, t: dict, rows: torch.Tensor) -> torch.Tensor:
+    """One bf16 row per sampled token: its outputs and the K/V page rows it wrote."""
+    n = rows.numel()
+    pages = t["kv_pool"][:, 0, t["block_mapping"][rows], :, t["slot_mapping"][rows], :]
+    parts = [outs["normed_in"][rows], outs["q"][rows].reshape(n, -1), outs["normed_post"][rows],
+             outs["residual"][rows], outs["act"][rows], pages[:, 0].reshape(n, -1),
+             pages[:, 1].reshape(n, -1)]
+    return torch.cat(parts, 1)
+
+
+def validate_layer(step: "Step", t: dict, batch, dev, rank: int, world: int,
+                   make_shard) -> dict | None:
+    """Every VALIDATE_EVERY-th token of the global batch (the ranks' batches in
+    rank order, rank r owning ``sharding.shard_range(world * T, world, r)``):
+    each rank runs one more step, takes its sampled tokens' outputs and K/V
+    page rows, and ``sharding.gather_rows`` (all-gather over NCCL) brings them
+    to rank 0.  Rank 0 regenerates each rank's seeded inputs with
+    ``make_shard(r)`` on its own GPU (the generator is the same on every
+    device) and checks every gathered row against the CPU oracle.  Returns
+    rank 0's summary (None on the other ranks)."""
+    from tinyserver_b200 import sharding
+
+    T = batch.num_tokens
+    G = world * T
+    glob = torch.arange(0, G, VALIDATE_EVERY)
+
+    def local_rows(r):
+        lo, hi = sharding.shard_range(G, world, r)
+        return (glob[(glob >= lo) & (glob < hi)] - lo).to(dev)
+
+    outs = step.run(t)
+    mine = _sample_rows(outs, t, local_rows(rank))
+    gathered = sharding.gather_rows(mine) if world > 1 else mine
+    torch.cuda.synchronize()
+    if rank != 0:
+        return None
+    s, dt = batch.cfg.shape, batch.cfg.dtype
+    widths = [s.hidden, s.num_q_heads * s.head_dim, s.hidden, s.hidden, s.intermediate,
+              s.num_kv_heads * s.head_dim, s.num_kv_heads * s.head_dim]
+    got_all = gathered.cpu()
+    checks = {name: {"ok": True, "bit_exact_min": 1.0, "max_abs_err": 0.0} for name in _OUT_ORDER}
+    at = 0
+    for r in range(world):
+        rows = local_rows(r)
+        tr = t if r == rank else make_shard(r).tensors
+        exp = _expected_rows(tr, rows, s, dt)
+        got = got_all[at:at + rows.numel()]
+        at += rows.numel()
+        col = 0
+        for name, w in zip(_OUT_ORDER, widths):
+            e = exp[name].reshape(rows.numel(), -1)
+            c = _within(got[:, col:col + w], e, exact=name in _EXACT)
+            col += w
+            agg = checks[name]
+            agg["ok"] = agg["ok"] and c["ok"]
+            agg["bit_exact_min"] = min(agg["bit_exact_min"], c["bit_exact"])
+            agg["max_abs_err"] = max(agg["max_abs_err"], c["max_abs_err"])
+        if r != rank:
+            del tr
+            torch.cuda.empty_cache()
+    return {"validated": all(c["ok"] for c in checks.values()), "rows_checked": int(at),
+            "ranks": world, "every": VALIDATE_EVERY, "checks": checks,
+            "how": "every 64th token of the global batch: outputs and written K/V page rows "
+                   "all-gathered to rank 0 (sharding.gather_rows over NCCL when N>1), checked "
+                   "against the CPU oracle on each rank's regenerated seeded inputs; residual "
+                   "and V pages bit-exact, the rest within |a-e| <= 2e-2 + 1e-2|e|"}
+
+
+# ----------------------------------------------------------------------------
+# the reference's own GPU path (baseline/reference_gpu.py)
+def reference_gpu_layer(batch, steps: int, ours_ms: float, local_rank: int,
+                        ours_outs: dict | None = None) -> dict:
+    """The reference's layer path (its transformers modules on CUDA and its
+    Triton KV store) over the same batch, timed like the headline."""
+    try:
+        from baseline import reference_gpu as R
+
+        t, s = batch.tensors, batch.cfg.shape
+        weights = {k: t[k] for k in ("embed_weight", "input_layernorm",
+                                     "post_attention_layernorm", "q_norm", "k_norm")}
+        ref = R.ReferenceGpuLayer(s, batch.cfg.dtype, weights)
+    except Exception as e:  # the reference or its Triton kernels are unavailable
+        return {"unavailable": f"{type(e).__name__}: {e}"}
+    args = (t["input_ids"], t["positions"], t["x_mlp"], t["qkv"], t["attn_out"], t["gate_up"],
+            t["k_cache"], t["v_cache"], t["block_mapping"], t["slot_mapping"])
+    ms, clocks = timed(lambda: ref.step(*args), max(3, min(steps, 50)), 3, local_rank)
+    T = batch.num_tokens
+    out = {"value": round(T / (ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 4),
+           "speedup_of_ours": round(ms / ours_ms, 2), "clocks": clocks,
+           "what": "the reference's path on this GPU: transformers 5.5.0 Qwen3 modules on CUDA "
+                   "(embedding, RMSNorm, rotary, apply_rotary_pos_emb, SiLU*up, eager) and the "
+                   "reference's Triton store_kv_cache_batched (server/model/kernels/kv_cache.py) "
+                   "with device mappings, from baseline/_ref"}
+    if ours_outs is not None:  # the two paths agree on this batch
+        normed, q, normed2, hidden, act = ref.step(*args)
+        T_ = q.shape[2]
+        mine = {"normed_in": normed[0], "q": q[0].transpose(0, 1).reshape(T_, -1, q.shape[-1]),
+                "normed_post": normed2[0], "residual": hidden[0], "act": act[0]}
+        agree = {k: _within(ours_outs[k].reshape(mine[k].shape), mine[k], exact=(k == "residual"))
+                 for k in mine}
+        out["agrees_with_ours"] = all(v["ok"] for v in agree.values())
+        out["agreement"] = {k: {"bit_exact": v["bit_exact"], "max_abs_err": v["max_abs_err"]}
+                            for k, v in agree.items()}
+    return out
+
+
+def _ref_timed(get_fn, call, steps: int, local_rank: int, ours_ms: float, unit_value) -> dict:
+    """Time one of the reference's GPU functions (``call(fn)`` per step)."""
+    try:
+        fn = get_fn()
+    except Exception as e:
+        return {"unavailable": f"{type(e).__name__}: {e}"}
+    ms, clocks = timed(lambda: call(fn), steps, 3, local_rank)
+    v, unit = unit_value(ms)
+    return {"value": round(v, 1), "unit": unit, "ms_per_step": round(ms, 4),
+            "speedup_of_ours": round(ms / ours_ms, 2), "clocks": clocks}
+
+
+# ----------------------------------------------------------------------------
 def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     from tinyserver_b200 import workloads as W
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    batch = W.make_batch(CONFIG, dev, shard=rank, max_tokens=args.max_tokens,
-                         num_blocks=args.num_blocks)
+    make = lambda r: W.make_batch(CONFIG, dev, shard=r, max_tokens=args.max_tokens,  # noqa
+                                  num_blocks=args.num_blocks)
+    batch = make(rank)
     t = batch.tensors
     T = batch.num_tokens
     step = Step(batch)
@@ -345,6 +560,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     del flush
     tsb.check_errors(dev)
 
+    # ---- outputs checked against the oracle (all ranks, outside the timing) --
+    validation = None
+    if not args.no_validate:
+        validation = validate_layer(step, t, batch, dev, rank, world, make)
+        if world > 1:
+            torch.distributed.barrier()
+
     # ---- end to end from pinned host buffers ----------------------------------
     e2e = None if args.no_e2e else measure_e2e(args, step, t, dev, world)
 
@@ -369,7 +591,6 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     attributed_ms = sum(per_kernel_us.values()) / 1e3
     dom = max(Step.KERNELS, key=lambda n: per_kernel_us[n])
     dom_gbs = bpt[dom] * T / (per_kernel_us[dom] * 1e-6) / 1e9
-    traffic = ncu_traffic(dom)
     line = {
         "metric": METRIC,
         "value": round(value, 1),
@@ -384,14 +605,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "dtype": "bf16",
         "data": "synthetic: seeded torch.Generator inputs of config c4's shapes and "
                 "distributions (no dataset or checkpoint)",
-        "config": {
-            "workload": "c4: Qwen3-8B layer, mixed 32x192 prefill + 2048 decode = "
-                        "8192 tokens/GPU, 16-token pages, 65536 blocks/GPU",
-            "tokens_per_gpu": T, "global_tokens": world * T, "hidden": 4096,
-            "num_q_heads": 32, "num_kv_heads": 8, "head_dim": 128, "intermediate": 12288,
-            "parallelism": f"token-sharded x{world}, no collective on the timed path",
-            "l2": f"inputs larger than L2: {step_bytes / 1e9:.2f} GB moved per step per GPU",
-        },
+        "config": layer_config(world, T, step_bytes),
         "hbm_gbs": round(step_bytes / (ms_per_step * 1e-3) / 1e9, 1),
         "hbm_frac": round(step_bytes / (ms_per_step * 1e-3) / 1e9 / peak, 4),
         "hbm_peak_gbs": peak,
@@ -405,16 +619,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                                  "a 256 MB read between launches so its inputs come from HBM; "
                                  "its own writes may end in L2 (in the step, the next kernel "
                                  "pays that write-back)",
-        "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(dom_gbs, 1),
-                     "peak": peak, "unit": "GB/s", "frac": round(dom_gbs / peak, 4),
-                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
-                     if peak_kind == "measured" else "fallback 6650 GB/s",
-                     "algorithmic_bytes_per_launch": bpt[dom] * T,
-                     "traffic": traffic},
+        "roofline": roofline("hbm", dom, dom_gbs, "GB/s", ncu_traffic(dom),
+                             algorithmic_bytes_per_launch=bpt[dom] * T),
         "gpu_launches": nk * args.steps,
         "pdl": "programmatic dependent launch between the step's kernels",
         "clocks": clocks,
         "e2e": None,
+        "validation": validation,
     }
     if e2e is not None:
         e2e_ms, e2e_steps, h2d, d2h = e2e
@@ -428,9 +639,207 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     if args.max_tokens is not None or args.num_blocks is not None:
         line["config"]["workload"] = (f"c4 prefix of {T} tokens, {batch.tensors['k_cache'].shape[0]}"
                                       "-block cache (a profiling case, not the benchmark workload)")
+    if world == 1 and not args.no_reference_gpu:
+        line["reference_gpu"] = reference_gpu_layer(batch, args.steps, ms_per_step, local_rank,
+                                                    step.run(t))
     if not args.no_cpu_baseline and world == 1:  # rank 0 at N=1 only
         line["cpu_baseline"] = cpu_baseline(batch, budget_s=args.cpu_seconds)
+    if world == 1 and not args.no_rows:
+        del step, t, batch
+        torch.cuda.empty_cache()
+        line["rows"] = run_rows(args, local_rank)
     return line
+
+
+def layer_config(world: int, T: int, step_bytes: int) -> dict:
+    return {
+        "workload": "c4: Qwen3-8B layer, mixed 32x192 prefill + 2048 decode = "
+                    "8192 tokens/GPU, 16-token pages, 65536 blocks/GPU",
+        "tokens_per_gpu": T, "global_tokens": world * T, "hidden": 4096,
+        "num_q_heads": 32, "num_kv_heads": 8, "head_dim": 128, "intermediate": 12288,
+        "block_size": 16, "num_blocks": 65536,
+        "parallelism": f"token-sharded x{world}, no collective on the timed path",
+        "l2": f"inputs larger than L2: {step_bytes / 1e9:.2f} GB moved per step per GPU",
+    }
+
+
+# ----------------------------------------------------------------------------
+# rows: the other configurations and the next rows of the path (N=1)
+def _compact(line: dict) -> dict:
+    keep = ("metric", "value", "unit", "ms_per_step", "us_per_step", "steps", "config",
+            "roofline", "clocks", "e2e", "cpu_baseline", "reference_gpu", "validation",
+            "graph", "kv_store", "gpu_launches", "dtype", "error")
+    return {k: line[k] for k in keep if k in line}
+
+
+def run_rows(args, local_rank: int) -> dict:
+    """Each row in turn on this GPU, its memory freed before the next; a row
+    that fails records its error and the others still run."""
+    rows = {}
+    for name, fn in (("c3_decode_step", row_c3_step), ("decode_attention", run_attention),
+                     ("prefill_attention", run_prefill), ("sampler", run_sample),
+                     ("c5_long_prefill", row_c5)):
+        try:
+            line = fn(args, 0, 1, local_rank, as_row=True)
+            rows[name] = _compact(line) if line is not None else None
+        except Exception as e:
+            rows[name] = {"error": f"{type(e).__name__}: {e}"}
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    return rows
+
+
+def row_c3_step(args, rank: int, world: int, local_rank: int, as_row: bool = False) -> dict:
+    """The fused-layer step on config c3: a continuous-batching decode step of
+    256 sequences (one token each, Qwen3-8B shapes, 32768-block cache).  Too
+    small to fill the GPU, so it is launch-bound: timed eagerly and as one
+    CUDA-graph replay per step (the way a serving loop would run it)."""
+    import tinyserver_b200 as tsb
+    from tinyserver_b200 import workloads as W
+
+    dev = torch.device("cuda", local_rank)
+    batch = W.make_batch("c3", dev, poison_cache=False)
+    t, T = batch.tensors, batch.num_tokens
+    step = Step(batch)
+    step_bytes = sum(step.bytes_per_token().values()) * T
+    n = 200
+    eager_ms, _ = timed(lambda: step.run(t), n, 5, local_rank)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            step.run(t)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        outs = step.run(t)
+    graph_ms, clocks = timed(g.replay, n, 5, local_rank)
+    tsb.check_errors(dev)
+    # every token of the step against the oracle
+    rows = torch.arange(T, device=dev)
+    exp = _expected_rows(t, rows, batch.cfg.shape, batch.cfg.dtype)
+    got = _sample_rows(outs, t, rows).cpu()
+    s = batch.cfg.shape
+    widths = [s.hidden, s.num_q_heads * s.head_dim, s.hidden, s.hidden, s.intermediate,
+              s.num_kv_heads * s.head_dim, s.num_kv_heads * s.head_dim]
+    col, checks = 0, {}
+    for name, w in zip(_OUT_ORDER, widths):
+        checks[name] = _within(got[:, col:col + w], exp[name].reshape(T, -1), name in _EXACT)
+        col += w
+    peak, _ = hbm_peak()
+    gbs = step_bytes / (graph_ms * 1e-3) / 1e9
+    ref = None
+    if not args.no_reference_gpu:
+        ref = reference_gpu_layer(batch, n, graph_ms, local_rank)
+    del g
+    return {
+        "metric": "fused-layer decode step tokens/s per B200 (c3, Qwen3-8B shapes)",
+        "value": round(T / (graph_ms * 1e-3), 1), "unit": "tokens/s",
+        "ms_per_step": round(graph_ms, 5), "us_per_step": round(1e3 * graph_ms, 2),
+        "steps": n, "dtype": "bf16",
+        "config": {"workload": "c3: 256 decode tokens, positions U[1, 8191], Qwen3-8B layer, "
+                               "32768-block cache", "tokens": T,
+                   "l2": f"{step_bytes / 1e6:.0f} MB per step: the step fits in L2 "
+                         "(decode steps are launch- and latency-bound)"},
+        "graph": {"us_per_step": round(1e3 * graph_ms, 2),
+                  "eager_us_per_step": round(1e3 * eager_ms, 2),
+                  "note": "value is the CUDA-graph replay of the five launches; eager is the "
+                          "same step launched from Python"},
+        "roofline": roofline("hbm", "whole step (5 kernels)", gbs, "GB/s",
+                             algorithmic_bytes_per_launch=step_bytes),
+        "clocks": clocks, "reference_gpu": ref,
+        "validation": {"validated": all(c["ok"] for c in checks.values()), "rows_checked": T,
+                       "checks": checks},
+        "gpu_launches": 5 * n,
+    }
+
+
+def row_c5(args, rank: int, world: int, local_rank: int, as_row: bool = False) -> dict:
+    """Config c5 at its full token count on one GPU: Qwen3-32B layer shapes,
+    4 x 32768-token prefill (131072 tokens), with the paged cache as large as
+    the GPU holds next to the step's tensors (up to the configuration's 1.835 M
+    blocks, 120 GB).  Also times the standalone KV store (this library's and
+    the reference's Triton kernel) into that cache."""
+    import tinyserver_b200 as tsb
+    from tinyserver_b200 import workloads as W
+
+    dev = torch.device("cuda", local_rank)
+    cfg = W.CONFIGS["c5"]
+    s = cfg.shape
+    T = 4 * 32768
+    elem = 2
+    inputs = (T * (3 * s.hidden + (s.num_q_heads + 2 * s.num_kv_heads) * s.head_dim
+                   + 2 * s.intermediate) + s.vocab * s.hidden) * elem
+    outputs = T * (5 * s.hidden + s.num_q_heads * s.head_dim + s.intermediate) * elem
+    block_bytes = 2 * s.num_kv_heads * cfg.block_size * s.head_dim * elem
+    free = torch.cuda.mem_get_info(dev)[0]
+    margin = 12 * 2 ** 30  # store sources, allocator slack, the oracle's sampled rows
+    blocks = int(min(cfg.num_blocks, (free - inputs - outputs - margin) // block_bytes))
+    if blocks < 8192 * 2:
+        raise MemoryError(f"c5: only {free / 1e9:.0f} GB free")
+    batch = W.make_batch(cfg, dev, num_blocks=blocks, poison_cache=False)
+    t = batch.tensors
+    step = Step(batch)
+    bpt = step.bytes_per_token()
+    step_bytes = sum(bpt.values()) * T
+    ms, clocks = timed(lambda: step.run(t), max(3, min(args.steps, 10)), 2, local_rank)
+    tsb.check_errors(dev)
+    # sampled rows against the oracle
+    rows = torch.arange(0, T, 512, device=dev)
+    exp = _expected_rows(t, rows, s, cfg.dtype)
+    got = _sample_rows(step.run(t), t, rows).cpu()
+    widths = [s.hidden, s.num_q_heads * s.head_dim, s.hidden, s.hidden, s.intermediate,
+              s.num_kv_heads * s.head_dim, s.num_kv_heads * s.head_dim]
+    col, checks = 0, {}
+    for name, w in zip(_OUT_ORDER, widths):
+        checks[name] = _within(got[:, col:col + w], exp[name].reshape(rows.numel(), -1),
+                               name in _EXACT)
+        col += w
+    del exp, got
+    # the standalone store (store_kv_cache_batched) into the same cache: K/V
+    # sources as the reference's caller makes them, (Hkv, T, D) contiguous
+    _, k, v = W.qkv_views(t["qkv"], s)
+    k_src, v_src = k.transpose(0, 1).contiguous(), v.transpose(0, 1).contiguous()
+    bm, sm = t["block_mapping"], t["slot_mapping"]
+    store_bytes = 4 * T * s.num_kv_heads * s.head_dim * elem + 16 * T
+    st_ms, st_clocks = timed(lambda: tsb.store_kv_cache_batched(k_src, v_src, t["k_cache"],
+                                                                 t["v_cache"], bm, sm),
+                             10, 3, local_rank)
+    tsb.check_errors(dev)
+    from baseline import reference_gpu as R
+    ref_store = _ref_timed(R.kv_store_batched,
+                           lambda fn: fn(k_src, v_src, t["k_cache"], t["v_cache"], bm, sm),
+                           10, local_rank, st_ms,
+                           lambda m: (store_bytes / (m * 1e-3) / 1e9, "GB/s"))
+    kv_store = {
+        "metric": "standalone store_kv_cache_batched GB/s (c5 K/V into the c5 cache)",
+        "us": round(1e3 * st_ms, 2),
+        "roofline": roofline("hbm", "kv_store_batched", store_bytes / (st_ms * 1e-3) / 1e9,
+                             "GB/s", algorithmic_bytes_per_launch=store_bytes),
+        "clocks": st_clocks, "reference_gpu": ref_store,
+        "note": "sources 2 x 268 MB (> L2), rows scattered over the whole cache; the "
+                "reference's Triton kernel gets the same tensors"}
+    peak, _ = hbm_peak()
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    return {
+        "metric": "fused-layer tokens/s and HBM GB/s per B200 (c5, Qwen3-32B shapes)",
+        "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 4),
+        "dtype": "bf16",
+        "config": {"workload": "c5: 4 x 32768-token prefill (131072 tokens) on one GPU, "
+                               f"Qwen3-32B layer, {blocks}-block cache "
+                               f"({blocks * block_bytes / 1e9:.0f} GB"
+                               + ("" if blocks == cfg.num_blocks else
+                                  f"; the configuration's {cfg.num_blocks} blocks do not fit "
+                                  "beside the step's tensors") + ")",
+                   "tokens": T, "num_blocks": blocks,
+                   "l2": f"{step_bytes / 1e9:.1f} GB moved per step (> L2)"},
+        "roofline": roofline("hbm", "whole step (5 kernels)", gbs, "GB/s",
+                             algorithmic_bytes_per_launch=step_bytes),
+        "clocks": clocks,
+        "validation": {"validated": all(c["ok"] for c in checks.values()),
+                       "rows_checked": int(rows.numel()), "every": 512, "checks": checks},
+        "kv_store": kv_store, "gpu_launches": 5,
+    }
 
 
 # ----------------------------------------------------------------------------
@@ -442,6 +851,15 @@ def _reference_inputs(batch, n_tokens: int, device="cpu"):
             "block_mapping", "slot_mapping"]
     out = {k: t[k][sl].to(device) for k in keys}
     return out
+
+
+def _cpu_cache(batch, dtype):
+    """K and V caches of the batch's full geometry (65536 blocks at c4) on the
+    host, left unfilled: the store touches only its rows, as on the GPU."""
+    s = batch.cfg.shape
+    N = batch.tensors["k_cache"].shape[0] if "k_cache" in batch.tensors else batch.cfg.num_blocks
+    kc = torch.empty(N, s.num_kv_heads, batch.cfg.block_size, s.head_dim, dtype=dtype)
+    return kc, torch.empty_like(kc)
 
 
 def cpu_baseline(batch, budget_s: float = 10.0, threads: int | None = None,
@@ -460,19 +878,15 @@ def cpu_baseline(batch, budget_s: float = 10.0, threads: int | None = None,
     for k in ("input_layernorm", "post_attention_layernorm", "q_norm", "k_norm"):
         weights[k] = t[k].to("cpu")
     ref = ReferenceLayerPath(s, batch.cfg.dtype, weights)
-    # a CPU cache large enough for the sample's slots (same page geometry)
     n = batch.num_tokens if max_tokens is None else min(max_tokens, batch.num_tokens)
     inp = _reference_inputs(batch, n)
     bm = inp.pop("block_mapping")
     sm = inp.pop("slot_mapping")
-    uniq, bm_local = torch.unique(bm, return_inverse=True)
-    kc = torch.zeros(len(uniq), s.num_kv_heads, batch.cfg.block_size, s.head_dim,
-                     dtype=batch.cfg.dtype)
-    vc = torch.zeros_like(kc)
+    kc, vc = _cpu_cache(batch, batch.cfg.dtype)
 
     def once():
         ref.step(inp["input_ids"], inp["positions"], inp["x_mlp"], inp["residual"], inp["qkv"],
-                 inp["attn_out"], inp["gate_up"], kc, vc, bm_local, sm)
+                 inp["attn_out"], inp["gate_up"], kc, vc, bm, sm)
 
     once()
     times = []
@@ -486,8 +900,8 @@ def cpu_baseline(batch, budget_s: float = 10.0, threads: int | None = None,
             "kind": "reference",
             "sample": f"{n} tokens of c4 per step, median of {len(times)} steps "
                       f"({sum(times):.1f} s); transformers {__import__('transformers').__version__}"
-                      " Qwen3 modules + torch index_put KV store, bf16, "
-                      f"torch.set_num_threads({threads})"}
+                      " Qwen3 modules + torch index_put KV store into the full "
+                      f"{kc.shape[0]}-block cache, bf16, torch.set_num_threads({threads})"}
 
 
 def run_reference(args, rank: int) -> dict | None:
@@ -506,18 +920,16 @@ def run_reference(args, rank: int) -> dict | None:
     weights = {k: t[k] for k in ("embed_weight", "input_layernorm", "post_attention_layernorm",
                                  "q_norm", "k_norm")}
     ref = ReferenceLayerPath(s, batch.cfg.dtype, weights)
+    kc, vc = t["k_cache"], t["v_cache"]  # the batch's own 65536-block cache
 
     def make(n):
         inp = _reference_inputs(batch, n)
         bm = inp.pop("block_mapping")
         sm = inp.pop("slot_mapping")
-        uniq, bm_local = torch.unique(bm, return_inverse=True)
-        kc = torch.zeros(len(uniq), s.num_kv_heads, batch.cfg.block_size, s.head_dim,
-                         dtype=batch.cfg.dtype)
-        return inp, kc, torch.zeros_like(kc), bm_local, sm
+        return inp, bm, sm
 
     def run(pack):
-        inp, kc, vc, bm, sm = pack
+        inp, bm, sm = pack
         ref.step(inp["input_ids"], inp["positions"], inp["x_mlp"], inp["residual"], inp["qkv"],
                  inp["attn_out"], inp["gate_up"], kc, vc, bm, sm)
 
@@ -539,20 +951,26 @@ def run_reference(args, rank: int) -> dict | None:
         times.append(time.perf_counter() - t0)
     total = sum(times)
     value = n * args.steps / total
+    bpt = W.bytes_per_token(s)
+    step_bytes = (sum(bpt.values()) + bpt["add_rmsnorm"]) * batch.num_tokens  # two add+norms
+    config = layer_config(1, batch.num_tokens, step_bytes)
+    config.pop("l2")
+    config.update({"workload": "c4: Qwen3-8B layer, mixed 32x192 prefill + 2048 decode = "
+                               f"8192 tokens/GPU; each step a {n}-token sample of that batch",
+                   "tokens_per_step": n, "parallelism": "host CPU, rank 0 only"})
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded torch.Generator inputs of config c4",
-        "config": {"workload": "c4: Qwen3-8B layer, mixed prefill+decode batch; each step a "
-                               f"{n}-token sample of the 8192-token batch",
-                   "tokens_per_step": n},
+        "config": config,
         "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": threads,
                          "kind": "reference",
                          "sample": f"{n} tokens of c4 per step on the host CPU: transformers "
-                                   "Qwen3 modules + torch index_put KV store (the reference's "
-                                   "Triton store has no CPU path)"},
+                                   "Qwen3 modules + torch index_put KV store into the full "
+                                   f"{kc.shape[0]}-block cache (the reference's Triton store "
+                                   "has no CPU path)"},
         "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -560,31 +978,53 @@ def run_reference(args, rank: int) -> dict | None:
 
 
 # ----------------------------------------------------------------------------
-def run_attention(args, rank: int, world: int, local_rank: int) -> dict | None:
-    """--workload attn: decode paged attention (the next row after the fused
-    path) on config c3: 256 sequences, one new token each at positions
-    U[1, 8191] (context = position + 1), Qwen3-8B heads (32 q / 8 kv,
-    head_dim 128), 16-token pages in a 32768-block cache, bf16.  Algorithmic
-    bytes: every context token's K and V row of every kv head once, plus q
-    and out."""
-    import tinyserver_b200 as tsb
+def decode_attention_batch(dev, rank: int = 0):
+    """Config c3's decode attention step with every sequence's context in
+    blocks of its own: 256 sequences, one new token each at positions
+    U[1, 8191] (context = position + 1), Qwen3-8B heads, 16-token pages.  The
+    cache has exactly the blocks the contexts need (a seeded permutation of
+    them), so no two sequences share a block and every K/V byte comes from
+    HBM once."""
     from tinyserver_b200 import workloads as W
+
+    cfg = W.CONFIGS["c3"]
+    s = cfg.shape
+    B = cfg.block_size
+    pos = torch.tensor([p for _, p in W.sequences(cfg, rank)])
+    lens = (pos + 1).to(torch.int32)
+    per = ((lens + B - 1) // B).tolist()
+    N = sum(per)
+    g = torch.Generator().manual_seed(W.seed_of(cfg, rank) + 23)
+    perm = torch.randperm(N, generator=g).to(torch.int32)
+    bt = torch.zeros(len(per), max(per), dtype=torch.int32)
+    at = 0
+    for i, n in enumerate(per):
+        bt[i, :n] = perm[at:at + n]
+        at += n
+    gd = torch.Generator(device=dev).manual_seed(W.seed_of(cfg, rank) + 5)
+    pool = torch.randn(2, N, s.num_kv_heads, B, s.head_dim, generator=gd, device=dev,
+                       dtype=torch.float32).to(cfg.dtype)
+    q = torch.randn(len(per), s.num_q_heads, s.head_dim, generator=gd, device=dev,
+                    dtype=torch.float32).to(cfg.dtype)
+    return cfg, q, pool, bt.to(dev), lens
+
+
+def run_attention(args, rank: int, world: int, local_rank: int, as_row: bool = False) -> dict | None:
+    """--workload attn: decode paged attention (the next row after the fused
+    path) on config c3's decode step with disjoint blocks (see
+    decode_attention_batch).  Algorithmic bytes: every context token's K and V
+    row of every kv head once, plus q, out and the block tables."""
+    import tinyserver_b200 as tsb
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    cfg = W.CONFIGS["c3"]
+    cfg, q, pool, bt, lens = decode_attention_batch(dev, rank)
     s = cfg.shape
-    b = W.index_data(cfg, shard=rank)
-    lens = (b.positions + 1).to(torch.int32)  # each sequence's one token attends to 0..pos
-    S, Hq, Hkv, D, B = len(b.seqs), s.num_q_heads, s.num_kv_heads, s.head_dim, cfg.block_size
-    g = torch.Generator(device=dev).manual_seed(W.seed_of(cfg, rank) + 5)
-    pool = torch.randn(2, cfg.num_blocks, Hkv, B, D, generator=g, device=dev,
-                       dtype=torch.float32).to(cfg.dtype)
-    q = torch.randn(S, Hq, D, generator=g, device=dev, dtype=torch.float32).to(cfg.dtype)
-    bt = b.block_tables.to(dev)
+    S, Hq, Hkv, D, B = q.shape[0], s.num_q_heads, s.num_kv_heads, s.head_dim, cfg.block_size
     sl = lens.to(dev)
     ws = torch.empty(tsb.paged_attention_workspace_bytes(S, Hq, D, bt.shape[1] * B) // 4 + 1,
                      dtype=torch.float32, device=dev)
+    steps = min(args.steps, 50) if as_row else args.steps
 
     def once():
         return tsb.paged_attention_forward(q, pool[0], pool[1], bt, B, sl, workspace=ws)
@@ -598,7 +1038,7 @@ def run_attention(args, rank: int, world: int, local_rank: int) -> dict | None:
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local_rank).start()
     e0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         once()
     e1.record()
     torch.cuda.synchronize()
@@ -609,6 +1049,7 @@ def run_attention(args, rank: int, world: int, local_rank: int) -> dict | None:
         m = torch.tensor([ms], device=dev, dtype=torch.float64)
         torch.distributed.all_reduce(m, op=torch.distributed.ReduceOp.MAX)
         ms = float(m.item())
+    per_ms = ms / steps
 
     # end to end: the step's queries, block tables and lengths from pinned host
     # memory, the output back; the KV cache is device state, as in the engine
@@ -627,7 +1068,7 @@ def run_attention(args, rank: int, world: int, local_rank: int) -> dict | None:
         for _ in range(3):
             e2e_once()
         torch.cuda.synchronize()
-        n_e2e = max(10, min(args.steps, 50))
+        n_e2e = max(10, min(steps, 50))
         a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a0.record()
         for _ in range(n_e2e):
@@ -643,14 +1084,16 @@ def run_attention(args, rank: int, world: int, local_rank: int) -> dict | None:
     if rank != 0:
         return None
     ctx = int(lens.sum())
+    nbytes = ctx * Hkv * D * 2 * 2 + 2 * S * Hq * D * 2 + S * (bt.shape[1] + 1) * 4
 
     # CPU baseline: the restated reference kernel on the host cores over
-    # groups of 8 sequences for about ten seconds, scaled to the batch by
+    # groups of 8 sequences for a bounded time, scaled to the batch by
     # context tokens (the work is one K and V row per context token)
     cpu = None
     if not args.no_cpu_baseline and world == 1:  # rank 0 at N=1 only
         from oracle import oracle
         kc, vc, qh, bth = pool[0].cpu(), pool[1].cpu(), q.cpu(), bt.cpu()
+        budget = min(args.cpu_seconds, 3.0 if as_row else 10.0)
         done, c0, i = 0, time.perf_counter(), 0
         while True:
             lo = (8 * i) % S
@@ -659,7 +1102,7 @@ def run_attention(args, rank: int, world: int, local_rank: int) -> dict | None:
             done += int(lens[lo:lo + 8].sum())
             i += 1
             secs = time.perf_counter() - c0
-            if secs > min(args.cpu_seconds, 10.0):
+            if secs > budget:
                 break
         rate = done / secs
         cpu = {"value": round(S / (ctx / rate), 1), "unit": "tokens/s",
@@ -667,37 +1110,35 @@ def run_attention(args, rank: int, world: int, local_rank: int) -> dict | None:
                "sample": f"{8 * i} sequences of the batch in groups of 8 ({done} context tokens "
                          f"in {secs:.1f} s), scaled to the batch's {ctx} context tokens; the "
                          "reference kernel's algorithm restated in torch on the host cores"}
-    peak, peak_kind = hbm_peak()
-    nbytes = ctx * Hkv * D * 2 * 2 + 2 * S * Hq * D * 2 + S * (bt.shape[1] + 1) * 4
-    per_ms = ms / args.steps
+    ref = None
+    if world == 1 and not args.no_reference_gpu:
+        from baseline import reference_gpu as R
+        ref = _ref_timed(R.paged_attention_forward,
+                         lambda fn: fn(q, pool[0], pool[1], bt, B, sl), 20, local_rank, per_ms,
+                         lambda m: (S / (m * 1e-3), "tokens/s"))
+        ref["what"] = ("the reference's Triton paged_attention_forward "
+                       "(server/model/kernels/paged_attention.py) on the same batch")
     gbs = nbytes / (per_ms * 1e-3) / 1e9
     return {
         "metric": "decode paged attention tokens/s and HBM GB/s per B200, Qwen3-8B heads",
         "value": round(world * S / (per_ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 4),
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded positions and cache contents of config c3",
         "config": {"workload": "c3 decode attention: 256 sequences x 1 token, context "
-                               f"{ctx} tokens in all, 16-token pages, 32768 blocks",
-                   "context_tokens": ctx, "l2": f"{nbytes / 1e9:.2f} GB read per step (> L2)"},
-        "roofline": {"bound": "hbm", "kernel": "paged_decode_mma_kernel + merge",
-                     "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(gbs / peak, 4), "algorithmic_bytes_per_launch": nbytes,
-                     "traffic": ncu_traffic("paged_attention")},
-        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 2 * args.steps, "clocks": clocks,
+                               f"{ctx} tokens in all, every sequence in blocks of its own "
+                               f"({pool.shape[1]} blocks of 16 tokens)",
+                   "context_tokens": ctx, "num_blocks": int(pool.shape[1]),
+                   "l2": f"{nbytes / 1e9:.2f} GB read per step (> L2), no block shared"},
+        "roofline": roofline("hbm", "paged_decode_mma_kernel + merge", gbs, "GB/s",
+                             ncu_traffic("paged_attention_disjoint"),
+                             algorithmic_bytes_per_launch=nbytes),
+        "cpu_baseline": cpu, "e2e": e2e, "reference_gpu": ref, "gpu_launches": 2 * steps,
+        "clocks": clocks,
     }
 
 
-def tensor_peak() -> tuple[float, str]:
-    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    try:
-        with open(p) as f:
-            return float(json.load(f)["bf16_tflops"]), "measured"
-    except (OSError, KeyError, ValueError):
-        return 1590.0, "fallback"
-
-
-def run_prefill(args, rank: int, world: int, local_rank: int) -> dict | None:
+def run_prefill(args, rank: int, world: int, local_rank: int, as_row: bool = False) -> dict | None:
     """--workload prefill: causal varlen prefill attention on config c2: 16
     packed sequences of U[128, 2048] tokens, Qwen3-1.7B heads (16 q / 8 kv,
     head_dim 128), bf16.  A contraction, so the roofline is the tensor-core
@@ -727,6 +1168,7 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> dict | None:
     cu = cu.to(dev)
     L = max(lens)
     step = [0]
+    steps = min(args.steps, 50) if as_row else args.steps
 
     def once():
         q, k, v = sets[step[0] % 2]
@@ -741,17 +1183,19 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> dict | None:
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local_rank).start()
     e0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         once()
     e1.record()
     torch.cuda.synchronize()
     clocks = sampler.stop()
     ms = e0.elapsed_time(e1)
+    tsb.check_errors(dev)
     if world > 1:
         m = torch.tensor([ms], device=dev, dtype=torch.float64)
         torch.distributed.all_reduce(m, op=torch.distributed.ReduceOp.MAX)
         ms = float(m.item())
     flops = sum(4 * D * n * (n + 1) // 2 for n in lens) * Hq
+    per_ms = ms / steps
 
     # end to end: q, k, v and cu_seqlens from pinned host memory, the output
     # back to pinned host memory, every step
@@ -771,7 +1215,7 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> dict | None:
         for _ in range(3):
             e2e_once()
         torch.cuda.synchronize()
-        n_e2e = max(10, min(args.steps, 20))
+        n_e2e = max(10, min(steps, 20))
         a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a0.record()
         for _ in range(n_e2e):
@@ -789,7 +1233,7 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     # CPU baseline: whole sequences of the batch, in order, through the
     # restatement of the reference's kernel (32-key blocks, torch on the host
-    # cores) for about ten seconds; FLOP rate scaled to the batch
+    # cores) for a bounded time; FLOP rate scaled to the batch
     cpu = None
     if not args.no_cpu_baseline and world == 1:  # rank 0 at N=1 only
         from oracle import oracle
@@ -797,6 +1241,7 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> dict | None:
         offs = [0]
         for n in lens:
             offs.append(offs[-1] + n)
+        budget = min(args.cpu_seconds, 3.0 if as_row else 10.0)
         done, c0, i = 0, time.perf_counter(), 0
         while True:
             n, o = lens[i % len(lens)], offs[i % len(lens)]
@@ -805,7 +1250,7 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> dict | None:
             done += 4 * D * n * (n + 1) // 2 * Hq
             i += 1
             secs = time.perf_counter() - c0
-            if secs > min(args.cpu_seconds, 10.0):
+            if secs > budget:
                 break
         rate = done / secs
         cpu = {"value": round(T / (flops / rate), 1), "unit": "tokens/s",
@@ -814,24 +1259,32 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> dict | None:
                          f"{secs:.1f} s, {rate / 1e9:.2f} GFLOP/s), scaled to the batch's "
                          f"{flops / 1e9:.0f} GFLOP; the reference kernel's algorithm restated "
                          "in torch on the host cores"}
-    per_ms = ms / args.steps
+    ref = None
+    if world == 1 and not args.no_reference_gpu:
+        from baseline import reference_gpu as R
+        q0, k0, v0 = sets[0]
+        ref = _ref_timed(R.flash_attn_varlen_func,
+                         lambda fn: fn(q0, k0, v0, cu, cu, L, L, True), 10, local_rank, per_ms,
+                         lambda m: (T / (m * 1e-3), "tokens/s"))
+        if "ms_per_step" in ref:
+            ref["tflops"] = round(flops / (ref["ms_per_step"] * 1e-3) / 1e12, 1)
+        ref["what"] = ("the reference's Triton flash_attn_varlen_func "
+                       "(server/model/kernels/varlen_attention.py) on the same batch")
     tf = flops / (per_ms * 1e-3) / 1e12
-    peak, kind = tensor_peak()
     return {
         "metric": "prefill varlen attention tokens/s and TFLOP/s per B200, Qwen3-1.7B heads",
         "value": round(world * T / (per_ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 4),
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded lengths and activations of config c2",
         "config": {"workload": f"c2 prefill attention: {len(lens)} sequences, {T} tokens, causal",
                    "tokens": T, "max_seqlen": L,
                    "l2": f"two input sets alternate: {2 * in_mb:.0f} MB of q/k/v between reuses "
                          f"> 126 MB L2"},
-        "roofline": {"bound": "tensor", "kernel": "varlen_attn_tc_kernel", "achieved": round(tf, 1),
-                     "peak": peak, "unit": "TFLOP/s", "frac": round(tf / peak, 4),
-                     "peak_source": f"{kind} bf16_tflops (cuBLAS burst)", "flops_per_launch": flops,
-                     "traffic": ncu_traffic("varlen_attn_tc_kernel")},
-        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks,
+        "roofline": roofline("tensor", "varlen_attn_tc_kernel", tf, "TFLOP/s",
+                             ncu_traffic("varlen_attn_tc_kernel"), flops_per_launch=flops),
+        "cpu_baseline": cpu, "e2e": e2e, "reference_gpu": ref, "gpu_launches": steps,
+        "clocks": clocks,
     }
 
 
@@ -845,7 +1298,7 @@ def _sample_inputs(B: int, V: int, seed: int, device) -> tuple:
     uniforms."""
     g = torch.Generator().manual_seed(seed)
     logits = (torch.randn(B, V, generator=g) * 4.0).to(torch.bfloat16)
-    pick = lambda vals: torch.tensor(vals)[torch.randint(0, len(vals), (B,), generator=g)]
+    pick = lambda vals: torch.tensor(vals)[torch.randint(0, len(vals), (B,), generator=g)]  # noqa
     temperature = pick([0.0, 0.6, 0.7, 0.8, 0.9, 1.0, 1.0, 1.2]).float()
     top_k = pick([0, 0, 20, 50, 1000]).long()
     top_p = pick([1.0, 0.9, 0.95, 0.95]).float()
@@ -854,7 +1307,7 @@ def _sample_inputs(B: int, V: int, seed: int, device) -> tuple:
             seeds.to(device), torch.full((B,), seed, dtype=torch.int64, device=device))
 
 
-def run_sample(args, rank: int, world: int, local_rank: int) -> dict | None:
+def run_sample(args, rank: int, world: int, local_rank: int, as_row: bool = False) -> dict | None:
     """--workload sample: the batched sampler after lm_head on a c3-sized
     decode step: 256 rows of Qwen3's 151936-token vocabulary, bf16 logits,
     mixed greedy / temperature / top-k / top-p rows, counter-hash noise fused
@@ -867,6 +1320,7 @@ def run_sample(args, rank: int, world: int, local_rank: int) -> dict | None:
     dev = torch.device("cuda", local_rank)
     B, V = args.sample_rows, SAMPLE_VOCAB
     sets = [_sample_inputs(B, V, 1000 * rank + i, dev) for i in range(3)]
+    steps = min(args.steps, 50) if as_row else args.steps
 
     def once(i):
         x, t, k, p, sd, st = sets[i % 3]
@@ -880,7 +1334,7 @@ def run_sample(args, rank: int, world: int, local_rank: int) -> dict | None:
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local_rank).start()
     e0.record()
-    for i in range(args.steps):
+    for i in range(steps):
         once(i)
     e1.record()
     torch.cuda.synchronize()
@@ -890,6 +1344,7 @@ def run_sample(args, rank: int, world: int, local_rank: int) -> dict | None:
         m = torch.tensor([ms], device=dev, dtype=torch.float64)
         torch.distributed.all_reduce(m, op=torch.distributed.ReduceOp.MAX)
         ms = float(m.item())
+    per_ms = ms / steps
 
     # end to end: logits from pinned host memory, tokens back to the host
     e2e = None
@@ -897,7 +1352,7 @@ def run_sample(args, rank: int, world: int, local_rank: int) -> dict | None:
         host = [s[0].cpu().pin_memory() for s in sets[:2]]
         dbuf = [torch.empty_like(s[0]) for s in sets[:2]]
         out_h = torch.empty(B, dtype=torch.int64).pin_memory()
-        n_e2e = max(10, min(args.steps, 50))
+        n_e2e = max(10, min(steps, 50))
         _, t, k, p, sd, st = sets[0]
         for i in range(3):
             dbuf[i % 2].copy_(host[i % 2], non_blocking=True)
@@ -924,37 +1379,43 @@ def run_sample(args, rank: int, world: int, local_rank: int) -> dict | None:
         n = 32
         u = oracle.uniforms_from_seeds(sd[:n].tolist(), st[:n].tolist())
         oracle.sample_tokens(x[:4], t[:4], k[:4], p[:4], u[:4])
+        budget = min(args.cpu_seconds, 3.0 if as_row else 10.0)
         c0 = time.perf_counter()
         reps = 0
         while True:
             oracle.sample_tokens(x[:n], t[:n], k[:n], p[:n], u)
             reps += 1
-            if time.perf_counter() - c0 > min(args.cpu_seconds, 10.0):
+            if time.perf_counter() - c0 > budget:
                 break
         cs = (time.perf_counter() - c0) / reps
         cpu = {"value": round(n / cs, 1), "unit": "rows/s", "cores": torch.get_num_threads(),
                "kind": "port", "sample": f"{n} rows of the same batch, {reps} repetitions, the "
                                          "reference's sort-based sample_tokens restated in torch "
                                          "on the host cores"}
-
-    per_ms = ms / args.steps
+    ref = None
+    if world == 1 and not args.no_reference_gpu:
+        from baseline import reference_gpu as R
+        x, t, k, p, sd, st = sets[0]
+        u = tsb.uniforms_from_seeds(sd, st)
+        ref = _ref_timed(R.sample_tokens, lambda fn: fn(x, t, k, p, u), 20, local_rank, per_ms,
+                         lambda m: (B / (m * 1e-3), "rows/s"))
+        ref["what"] = ("the reference's sample_tokens (server/model/sampling.py, torch sort, "
+                       "softmax and cumsum on the GPU) on the same logits and uniforms")
     nbytes = B * V * 2 + B * (4 + 8 + 4 + 8 + 8 + 8)
     gbs = nbytes / (per_ms * 1e-3) / 1e9
-    peak, kind = hbm_peak()
     return {
         "metric": "sampled rows/s per B200 (Qwen3 vocabulary, top-k/top-p/temperature mix)",
         "value": round(world * B / (per_ms * 1e-3), 1), "unit": "rows/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 4),
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: seeded bf16 logits N(0, 16), mixed per-row sampling settings",
         "config": {"workload": f"c3 decode step sampling: {B} rows x {V} vocab, bf16 logits"
                                + ("" if B == SAMPLE_ROWS else " (a profiling case, not the benchmark)"),
                    "rows": B, "vocab": V, "l2": "3 rotating logits buffers (233 MB > L2)"},
-        "roofline": {"bound": "hbm", "kernel": "sample_kernel", "achieved": round(gbs, 1),
-                     "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
-                     "peak_source": f"{kind} hbm_gbs", "bytes_per_launch": nbytes,
-                     "traffic": ncu_traffic("sample_kernel")},
-        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks,
+        "roofline": roofline("hbm", "sample_kernel", gbs, "GB/s", ncu_traffic("sample_kernel"),
+                             bytes_per_launch=nbytes),
+        "cpu_baseline": cpu, "e2e": e2e, "reference_gpu": ref, "gpu_launches": steps,
+        "clocks": clocks,
     }
 
 
@@ -967,6 +1428,12 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
+    ap.add_argument("--no-validate", action="store_true",
+                    help="skip the check of sampled outputs against the oracle")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's own GPU code")
+    ap.add_argument("--no-rows", action="store_true",
+                    help="skip the other configurations and rows (N=1 only)")
     ap.add_argument("--max-tokens", type=int, default=None,
                     help="keep a prefix of the batch (small profiling cases only)")
     ap.add_argument("--num-blocks", type=int, default=None,
@@ -977,10 +1444,11 @@ def main() -> None:
                     help="total CPU time budget of the --impl reference run")
     ap.add_argument("--sample-rows", type=int, default=SAMPLE_ROWS,
                     help="rows of --workload sample (small profiling cases only)")
-    ap.add_argument("--workload", choices=["layer", "attn", "prefill", "sample"],
+    ap.add_argument("--workload", choices=["layer", "attn", "prefill", "sample", "c3", "c5"],
                     default="layer",
                     help="layer: the fused-layer step (the headline); attn: decode attention; "
-                         "prefill: varlen prefill attention; sample: the batched sampler")
+                         "prefill: varlen prefill attention; sample: the batched sampler; "
+                         "c3 / c5: the fused step on those configurations")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -998,14 +1466,15 @@ def main() -> None:
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
     try:
-        if args.workload == "attn":
-            line = run_attention(args, rank, world, local_rank)
-        elif args.workload == "prefill":
-            line = run_prefill(args, rank, world, local_rank)
-        elif args.workload == "sample":
-            line = run_sample(args, rank, world, local_rank)
-        else:
+        fn = {"attn": run_attention, "prefill": run_prefill, "sample": run_sample,
+              "c3": row_c3_step, "c5": row_c5}.get(args.workload)
+        if fn is None:
             line = run_ours(args, rank, world, local_rank)
+        elif args.workload in ("c3", "c5"):
+            torch.cuda.set_device(local_rank)
+            line = fn(args, rank, world, local_rank) if rank == 0 else None
+        else:
+            line = fn(args, rank, world, local_rank)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()

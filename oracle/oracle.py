@@ -1,8 +1,9 @@
 """ctypes front end of the C oracle (``qwen3_oracle.c``).
 
 TEST INFRASTRUCTURE ONLY: the parity checker for tinyserver_b200's CUDA path.
-Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
-leg may import this module.  The product never does.
+Only ``tests/``, ``__graft_entry__.smoke()``, ``bench.py``'s CPU-baseline leg
+and ``bench.py``'s validation of sampled outputs (the checker's role, outside
+every timed region) may import this module.  The product never does.
 
 Every function takes and returns CPU torch tensors and mirrors one op of the
 reference path (citations are in the C source):

@@ -107,3 +107,17 @@ def assert_untouched(pool: torch.Tensor, snapshot: torch.Tensor, block_mapping: 
             diff = (a != e).nonzero()[0].tolist()
             diff[2] += b0
             raise AssertionError(f"an unwritten cache element changed, first at pool index {diff}")
+
+
+def reference_module(name: str):
+    """Import a module of the reference itself (e.g. ``server.model.patches.qwen3``)
+    from its offline install in baseline/_ref, or the directory TINYSERVER_REF
+    names; the calling test is skipped, with the reason, when neither holds it."""
+    import pytest
+
+    from baseline.reference_gpu import load
+
+    try:
+        return load(name)
+    except ImportError as e:
+        pytest.skip(f"the reference is not importable here: {e}")

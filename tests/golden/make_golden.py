@@ -1,10 +1,10 @@
 """Generate the golden fixtures in tests/golden/ from the reference's own code.
 
-Run in a container that has the reference checkout (default path below, or
-``TINYSERVER_REF``); the GPU box never runs this script, it only reads the
-fixtures it wrote::
+Run in a container that has the reference checkout, named by ``--ref`` or
+``TINYSERVER_REF`` (the script stops with a message when neither is given);
+the GPU box never runs this script, it only reads the fixtures it wrote::
 
-    python tests/golden/make_golden.py [--ref /path/to/tinyserver]
+    python tests/golden/make_golden.py --ref /path/to/tinyserver
 
 What produces the golden outputs:
 
@@ -476,9 +476,13 @@ def _sampling_case() -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("TINYSERVER_REF", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("TINYSERVER_REF"),
+                    help="the reference checkout (default: $TINYSERVER_REF)")
     ap.add_argument("--only", default=None, help="write just this fixture (e.g. paged_attention)")
     args = ap.parse_args()
+    if not args.ref or not os.path.isdir(os.path.join(args.ref, "server", "model")):
+        ap.error("give the reference checkout with --ref or TINYSERVER_REF (a directory that "
+                 "holds server/model)")
     sys.path.insert(0, args.ref)
     import transformers
     torch.manual_seed(0)

@@ -71,3 +71,20 @@ def test_operator_overrides_rebind_and_restore():
     finally:
         patches.restore_operator_overrides()
     assert hf.apply_rotary_pos_emb is original
+
+
+def test_fused_forward_drops_the_cached_mapping_of_a_reused_context():
+    """A context object reused across forwards: the fused model forward drops
+    the batch mapping cached on it before its layers run, so a stale mapping
+    (same position_ids address, different sequences) is never served."""
+    from tests.qwen3_tiny import Context
+
+    model = tiny_model(dtype=torch.float32)
+    patches.allocate_kv_cache(model, num_blocks=8, block_size=16, dtype=torch.float32,
+                              device="cpu")
+    ctx = Context(mode="prefill", sequences=[{"num_tokens": 4, "block_table": [0]}])
+    ctx._tinyserver_b200_mapping = "stale"
+    patches.install_fused(model, context=lambda: ctx, attention=object())
+    with pytest.raises(ValueError, match="CUDA tensors only"):  # the first op needs a GPU
+        model.model(input_ids=torch.zeros(1, 4, dtype=torch.long), use_cache=False)
+    assert ctx._tinyserver_b200_mapping is None

@@ -49,7 +49,7 @@ from ..kernels import kv_cache as KV
 __all__ = ["AttentionBackend", "FusedDecodeAttention", "ReferenceAttention", "install_fused",
            "fused_qwen3_model_loader",
            "install_operator_overrides", "restore_operator_overrides", "allocate_kv_cache",
-           "batch_mapping"]
+           "batch_mapping", "forget_batch_mapping"]
 
 
 # ----------------------------------------------------------------------------
@@ -103,7 +103,7 @@ def _decoder_layer_forward(layer: torch.nn.Module) -> Callable[..., torch.Tensor
     return forward
 
 
-def _model_forward(base: torch.nn.Module) -> Callable[..., Any]:
+def _model_forward(base: torch.nn.Module, context: Callable[[], Any]) -> Callable[..., Any]:
     """Qwen3Model.forward (modeling_qwen3.py:378-437) for the paged serving path,
     with every residual add fused into the norm that follows it: the
     post-attention add into post_attention_layernorm, and the end-of-layer add
@@ -111,7 +111,9 @@ def _model_forward(base: torch.nn.Module) -> Callable[..., Any]:
     after the last layer.  That removes one full read and write of the hidden
     state per layer against running the decoder layers one by one.  The
     causal masks are not built: the paged attention, like the reference's
-    (qwen3.py:216-418), never reads them."""
+    (qwen3.py:216-418), never reads them.  Each call first drops the batch
+    mapping cached on the inference context, so the layers of this forward
+    build it once from this forward's context."""
     from transformers.modeling_outputs import BaseModelOutputWithPast
 
     layers = list(base.layers[: base.config.num_hidden_layers])
@@ -125,6 +127,7 @@ def _model_forward(base: torch.nn.Module) -> Callable[..., Any]:
         if use_cache or past_key_values is not None:
             raise ValueError("the fused paged model keeps its own paged KV cache: call it "
                              "with use_cache=False and no past_key_values")
+        forget_batch_mapping(context())
         hidden = base.embed_tokens(input_ids) if inputs_embeds is None else inputs_embeds
         if position_ids is None:
             position_ids = torch.arange(hidden.shape[1], device=hidden.device).unsqueeze(0)
@@ -245,7 +248,16 @@ def batch_mapping(ctx: Any, position_ids: torch.Tensor, block_size: int) -> Batc
     restart at 0 per sequence, prefill_helpers.py:27) and of its decode
     stores (kv_cache.py:49-58 with start_position = position_ids[0, i]).
     Built with one host->device copy of the block tables and one kernel,
-    cached on the context object, so every layer of the forward reuses it."""
+    cached on the context object, so every layer of the forward reuses it.
+
+    The cache key is the identity of ``position_ids`` (address, version,
+    size) and the mode, not the sequences' contents.  The fused model forward
+    drops the cache when it starts (:func:`forget_batch_mapping`), so a
+    context object reused from one forward to the next is rebuilt for each.
+    A caller that runs the attention layers without that model forward and
+    reuses one context object must make a new context per step, as the
+    reference's engine does (engine.py:579-582), or call
+    :func:`forget_batch_mapping` between steps."""
     dev = position_ids.device
     key = (position_ids.data_ptr(), position_ids._version, position_ids.numel(), ctx.mode,
            block_size)
@@ -278,6 +290,15 @@ def batch_mapping(ctx: Any, position_ids: torch.Tensor, block_size: int) -> Batc
     except AttributeError:  # a context type with __slots__: rebuild per layer
         pass
     return m
+
+
+def forget_batch_mapping(ctx: Any) -> None:
+    """Drop the batch mapping cached on an inference context (if any)."""
+    if getattr(ctx, "_tinyserver_b200_mapping", None) is not None:
+        try:
+            setattr(ctx, "_tinyserver_b200_mapping", None)
+        except AttributeError:
+            pass
 
 
 def _paged_attention_forward(attn: torch.nn.Module, context: Callable[[], Any],
@@ -375,7 +396,7 @@ def install_fused(model: torch.nn.Module, *, paged: bool | None = None,
                                  "(allocate the cache first)")
             attn._tinyserver_b200_inv_freq = inv_freq
             attn.forward = _paged_attention_forward(attn, ctx, backend)
-        base.forward = _model_forward(base)
+        base.forward = _model_forward(base, ctx)
     return model
 
 
