@@ -8,7 +8,6 @@ fails, every op raises -- there is no CPU or torch fallback.
 from __future__ import annotations
 
 import ctypes
-import hashlib
 import os
 import threading
 
@@ -155,33 +154,11 @@ _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
 
 
-def _source_hash() -> str:
-    h = hashlib.sha256()
-    for p in sorted(_build._deps()):
-        h.update(os.path.basename(p).encode())
-        with open(p, "rb") as f:
-            h.update(f.read())
-    return h.hexdigest()
-
-
-def _stamp_path() -> str:
-    return _build.LIB + ".srchash"
-
-
 def ensure_built() -> str:
-    """Return the library path, (re)building it when its sources changed.
-
-    Staleness is decided by a hash of the sources (not mtimes, which a copy of
-    the tree to another machine does not preserve)."""
-    want = _source_hash()
-    stamp = _stamp_path()
-    if os.path.exists(_build.LIB) and os.path.exists(stamp):
-        with open(stamp) as f:
-            if f.read().strip() == want:
-                return _build.LIB
-    _build.build(force=True)
-    with open(stamp, "w") as f:
-        f.write(want)
+    """Return the library path, (re)building it when its sources changed (the
+    sources' hash decides; concurrent processes take turns, see build.build)."""
+    if _build.is_stale():
+        _build.build()
     return _build.LIB
 
 

@@ -12,7 +12,9 @@ from __future__ import annotations
 
 import argparse
 import concurrent.futures as cf
+import fcntl
 import glob
+import hashlib
 import os
 import shutil
 import subprocess
@@ -45,11 +47,27 @@ def _deps() -> list[str]:
         glob.glob(os.path.join(INCLUDE, "*.h"))
 
 
+def source_hash() -> str:
+    """Hash of every source the library is built from (file names and bytes)."""
+    h = hashlib.sha256()
+    for p in sorted(_deps()):
+        h.update(os.path.basename(p).encode())
+        with open(p, "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()
+
+
+STAMP = LIB + ".srchash"
+
+
 def is_stale() -> bool:
-    if not os.path.exists(LIB):
+    """Whether the library is missing or was built from other sources.  The
+    sources' hash decides, not mtimes, which a copy of the tree to another
+    machine does not preserve."""
+    if not os.path.exists(LIB) or not os.path.exists(STAMP):
         return True
-    t = os.path.getmtime(LIB)
-    return any(os.path.getmtime(p) > t for p in _deps())
+    with open(STAMP) as f:
+        return f.read().strip() != source_hash()
 
 
 def _compile(src: str, verbose_ptxas: bool) -> str:
@@ -66,19 +84,27 @@ def _compile(src: str, verbose_ptxas: bool) -> str:
 
 
 def build(force: bool = False, verbose_ptxas: bool = False) -> str:
-    """Compile every csrc/*.cu for sm_100a and link the shared library."""
-    if not force and not verbose_ptxas and not is_stale():
-        return LIB
+    """Compile every csrc/*.cu for sm_100a and link the shared library, then
+    record the sources' hash beside it.  Processes that build at the same time
+    (the ranks of one job) take turns on a file lock, and a process that gets
+    the lock after another built the same sources does nothing."""
     os.makedirs(BUILD, exist_ok=True)
     os.makedirs(os.path.dirname(LIB), exist_ok=True)
-    with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
-        objs = list(ex.map(lambda s: _compile(s, verbose_ptxas), sources()))
-    tmp = LIB + ".tmp"
-    cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs]
-    r = subprocess.run(cmd, capture_output=True, text=True)
-    if r.returncode != 0:
-        raise RuntimeError(f"nvcc link failed:\n{r.stdout}\n{r.stderr}")
-    os.replace(tmp, LIB)
+    with open(LIB + ".lock", "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        if not force and not verbose_ptxas and not is_stale():
+            return LIB
+        want = source_hash()
+        with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
+            objs = list(ex.map(lambda s: _compile(s, verbose_ptxas), sources()))
+        tmp = f"{LIB}.tmp{os.getpid()}"
+        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc link failed:\n{r.stdout}\n{r.stderr}")
+        os.replace(tmp, LIB)
+        with open(STAMP, "w") as f:
+            f.write(want)
     return LIB
 
 
