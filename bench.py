@@ -162,6 +162,23 @@ def timed(fn, steps: int, warmup: int, device_index: int) -> tuple[float, dict]:
     return total_ms / n, sampler.stop()
 
 
+def event_loop(fn, steps: int, min_seconds: float = 0.0) -> tuple[float, int]:
+    """Rounds of ``steps`` back-to-back calls between two CUDA events on the
+    current stream, repeated until ``min_seconds`` have passed (so the clock
+    sampler sees the timed region); returns (total ms, total calls)."""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    total_ms, n, t_end = 0.0, 0, time.perf_counter() + min_seconds
+    while n == 0 or time.perf_counter() < t_end:
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        total_ms += e0.elapsed_time(e1)
+        n += steps
+    return total_ms, n
+
+
 def roofline(bound: str, kernel: str, achieved: float, unit: str, traffic=None, **extra) -> dict:
     peak, kind = hbm_peak() if bound == "hbm" else tensor_peak()
     src = "hbm_gbs" if bound == "hbm" else "bf16_tflops (cuBLAS burst)"
@@ -668,7 +685,7 @@ def layer_config(world: int, T: int, step_bytes: int) -> dict:
 def _compact(line: dict) -> dict:
     keep = ("metric", "value", "unit", "ms_per_step", "us_per_step", "steps", "config",
             "roofline", "clocks", "e2e", "cpu_baseline", "reference_gpu", "validation",
-            "graph", "kv_store", "gpu_launches", "dtype", "error")
+            "graph", "kv_store", "gpu_launches", "dtype", "e2e_note", "error")
     return {k: line[k] for k in keep if k in line}
 
 
@@ -732,6 +749,12 @@ def row_c3_step(args, rank: int, world: int, local_rank: int, as_row: bool = Fal
     if not args.no_reference_gpu:
         ref = reference_gpu_layer(batch, n, graph_ms, local_rank)
     del g
+    e2e = None
+    if not args.no_e2e:  # eager, through the public API, host buffers every step
+        e2e_ms, e2e_steps, h2d, d2h = measure_e2e(args, step, t, dev, 1)
+        e2e = {"value": round(T * e2e_steps / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps}
+    cpu = None if args.no_cpu_baseline else cpu_baseline(batch, budget_s=min(args.cpu_seconds, 3.0))
     return {
         "metric": "fused-layer decode step tokens/s per B200 (c3, Qwen3-8B shapes)",
         "value": round(T / (graph_ms * 1e-3), 1), "unit": "tokens/s",
@@ -747,7 +770,7 @@ def row_c3_step(args, rank: int, world: int, local_rank: int, as_row: bool = Fal
                           "same step launched from Python"},
         "roofline": roofline("hbm", "whole step (5 kernels)", gbs, "GB/s",
                              algorithmic_bytes_per_launch=step_bytes),
-        "clocks": clocks, "reference_gpu": ref,
+        "clocks": clocks, "reference_gpu": ref, "e2e": e2e, "cpu_baseline": cpu,
         "validation": {"validated": all(c["ok"] for c in checks.values()), "rows_checked": T,
                        "checks": checks},
         "gpu_launches": 5 * n,
@@ -819,7 +842,10 @@ def row_c5(args, rank: int, world: int, local_rank: int, as_row: bool = False) -
         "clocks": st_clocks, "reference_gpu": ref_store,
         "note": "sources 2 x 268 MB (> L2), rows scattered over the whole cache; the "
                 "reference's Triton kernel gets the same tensors"}
-    peak, _ = hbm_peak()
+    cpu = None
+    if not args.no_cpu_baseline:
+        cpu = cpu_baseline(batch, budget_s=min(args.cpu_seconds, 3.0), max_tokens=2048,
+                           compact_cache=True)
     gbs = step_bytes / (ms * 1e-3) / 1e9
     return {
         "metric": "fused-layer tokens/s and HBM GB/s per B200 (c5, Qwen3-32B shapes)",
@@ -838,7 +864,8 @@ def row_c5(args, rank: int, world: int, local_rank: int, as_row: bool = False) -
         "clocks": clocks,
         "validation": {"validated": all(c["ok"] for c in checks.values()),
                        "rows_checked": int(rows.numel()), "every": 512, "checks": checks},
-        "kv_store": kv_store, "gpu_launches": 5,
+        "kv_store": kv_store, "gpu_launches": 5, "cpu_baseline": cpu,
+        "e2e_note": "no end-to-end leg at c5: a step's host buffers would be ~34 GB",
     }
 
 
@@ -853,21 +880,24 @@ def _reference_inputs(batch, n_tokens: int, device="cpu"):
     return out
 
 
-def _cpu_cache(batch, dtype):
+def _cpu_cache(batch, dtype, num_blocks: int | None = None):
     """K and V caches of the batch's full geometry (65536 blocks at c4) on the
     host, left unfilled: the store touches only its rows, as on the GPU."""
     s = batch.cfg.shape
-    N = batch.tensors["k_cache"].shape[0] if "k_cache" in batch.tensors else batch.cfg.num_blocks
+    N = num_blocks or (batch.tensors["k_cache"].shape[0] if "k_cache" in batch.tensors
+                       else batch.cfg.num_blocks)
     kc = torch.empty(N, s.num_kv_heads, batch.cfg.block_size, s.head_dim, dtype=dtype)
     return kc, torch.empty_like(kc)
 
 
 def cpu_baseline(batch, budget_s: float = 10.0, threads: int | None = None,
-                 max_tokens: int | None = None) -> dict:
+                 max_tokens: int | None = None, compact_cache: bool = False) -> dict:
     """Time the reference's CPU path (transformers modules + index_put store) on
     the batch (or its first ``max_tokens`` tokens) for about ``budget_s``
     seconds; returns tokens/s.  The whole batch by default: a small sample
-    would sit in the host caches and flatter the CPU."""
+    would sit in the host caches and flatter the CPU.  ``compact_cache``
+    stores into a cache of only the sample's blocks (for caches too large for
+    host memory, c5's 120 GB)."""
     from oracle.ref_torch_cpu import ReferenceLayerPath
 
     threads = threads or os.cpu_count() or 1
@@ -882,7 +912,11 @@ def cpu_baseline(batch, budget_s: float = 10.0, threads: int | None = None,
     inp = _reference_inputs(batch, n)
     bm = inp.pop("block_mapping")
     sm = inp.pop("slot_mapping")
-    kc, vc = _cpu_cache(batch, batch.cfg.dtype)
+    if compact_cache:
+        uniq, bm = torch.unique(bm, return_inverse=True)
+        kc, vc = _cpu_cache(batch, batch.cfg.dtype, num_blocks=len(uniq))
+    else:
+        kc, vc = _cpu_cache(batch, batch.cfg.dtype)
 
     def once():
         ref.step(inp["input_ids"], inp["positions"], inp["x_mlp"], inp["residual"], inp["qkv"],
@@ -896,12 +930,14 @@ def cpu_baseline(batch, budget_s: float = 10.0, threads: int | None = None,
         once()
         times.append(time.perf_counter() - t0)
     med = statistics.median(times)
+    cache = (f"a {kc.shape[0]}-block cache of only the sample's blocks" if compact_cache
+             else f"the full {kc.shape[0]}-block cache")
     return {"value": round(n / med, 1), "unit": "tokens/s", "cores": threads,
             "kind": "reference",
-            "sample": f"{n} tokens of c4 per step, median of {len(times)} steps "
+            "sample": f"{n} tokens of {batch.cfg.name} per step, median of {len(times)} steps "
                       f"({sum(times):.1f} s); transformers {__import__('transformers').__version__}"
-                      " Qwen3 modules + torch index_put KV store into the full "
-                      f"{kc.shape[0]}-block cache, bf16, torch.set_num_threads({threads})"}
+                      f" Qwen3 modules + torch index_put KV store into {cache}, bf16, "
+                      f"torch.set_num_threads({threads})"}
 
 
 def run_reference(args, rank: int) -> dict | None:
@@ -1035,15 +1071,9 @@ def run_attention(args, rank: int, world: int, local_rank: int, as_row: bool = F
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local_rank).start()
-    e0.record()
-    for _ in range(steps):
-        once()
-    e1.record()
-    torch.cuda.synchronize()
+    ms, steps = event_loop(once, steps, 0.25 if as_row else 0.0)
     clocks = sampler.stop()
-    ms = e0.elapsed_time(e1)
     tsb.check_errors(dev)
     if world > 1:
         m = torch.tensor([ms], device=dev, dtype=torch.float64)
@@ -1180,15 +1210,9 @@ def run_prefill(args, rank: int, world: int, local_rank: int, as_row: bool = Fal
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local_rank).start()
-    e0.record()
-    for _ in range(steps):
-        once()
-    e1.record()
-    torch.cuda.synchronize()
+    ms, steps = event_loop(once, steps, 0.25 if as_row else 0.0)
     clocks = sampler.stop()
-    ms = e0.elapsed_time(e1)
     tsb.check_errors(dev)
     if world > 1:
         m = torch.tensor([ms], device=dev, dtype=torch.float64)
@@ -1331,15 +1355,15 @@ def run_sample(args, rank: int, world: int, local_rank: int, as_row: bool = Fals
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local_rank).start()
-    e0.record()
-    for i in range(steps):
-        once(i)
-    e1.record()
-    torch.cuda.synchronize()
+    counter = [0]
+
+    def next_step():
+        once(counter[0])
+        counter[0] += 1
+
+    ms, steps = event_loop(next_step, steps, 0.25 if as_row else 0.0)
     clocks = sampler.stop()
-    ms = e0.elapsed_time(e1)
     if world > 1:
         m = torch.tensor([ms], device=dev, dtype=torch.float64)
         torch.distributed.all_reduce(m, op=torch.distributed.ReduceOp.MAX)
