@@ -55,11 +55,14 @@ __device__ __forceinline__ float rnd<float>(float v) {
 }
 
 // ---------------------------------------------------------------------------
-// 16-byte global memory access.  Streamed data (read once) bypasses L1 and
-// asks L2 for a 256-byte prefetch; streamed outputs are marked evict-first.
+// 16-byte global memory access.  Streamed data (read once) is read through
+// the non-coherent read-only path with no cache hint: on B200 the c4 step ran
+// 242.7 us with L1::no_allocate + L2::256B on these loads and 235.4 us
+// without (every kernel faster; L1::evict_first measured like no_allocate).
+// Streamed outputs are marked evict-first.
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
     uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
                  : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                  : "l"(p));
     return r;
@@ -67,7 +70,7 @@ __device__ __forceinline__ uint4 ld_stream16(const void* p) {
 
 __device__ __forceinline__ uint2 ld_stream8(const void* p) {
     uint2 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];"
+    asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];"
                  : "=r"(r.x), "=r"(r.y)
                  : "l"(p));
     return r;
