@@ -512,18 +512,18 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     import tinyserver_b200 as tsb
     tsb.load_library()
+
+    # ---- device-resident timing: the headline --------------------------------
+    # W warm-up steps run right before the timed ones, so the GPU is busy (and
+    # at its working clocks) up to the start of the timed region; then K steps
+    # back to back between two events.  Nothing is recorded between the
+    # kernels, so consecutive launches keep their programmatic-dependent-launch
+    # overlap.  The clocks are sampled every 2 ms over the whole stretch.
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local_rank, interval=0.002).start()
     for _ in range(max(args.warmup, 3)):
         step.run(t)
     tsb.check_errors(dev)
-    torch.cuda.synchronize()
-
-    # ---- device-resident timing: the headline --------------------------------
-    # K steps back to back between two events; nothing is recorded between
-    # the kernels, so consecutive launches keep their programmatic-dependent-
-    # launch overlap.
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(local_rank).start()
-    time.sleep(0.05)
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
