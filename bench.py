@@ -413,6 +413,13 @@ def validate_layer(step: "Step", t: dict, batch, dev, rank: int, world: int,
     torch.cuda.synchronize()
     if rank != 0:
         return None
+    res = guarded(_check_gathered, gathered, t, batch, rank, world, local_rows, make_shard)
+    res.setdefault("validated", False)
+    return res
+
+
+def _check_gathered(gathered, t, batch, rank, world, local_rows, make_shard) -> dict:
+    """Rank 0's half of validate_layer: every gathered row against the oracle."""
     s, dt = batch.cfg.shape, batch.cfg.dtype
     widths = [s.hidden, s.num_q_heads * s.head_dim, s.hidden, s.hidden, s.intermediate,
               s.num_kv_heads * s.head_dim, s.num_kv_heads * s.head_dim]
@@ -657,13 +664,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         line["config"]["workload"] = (f"c4 prefix of {T} tokens, {batch.tensors['k_cache'].shape[0]}"
                                       "-block cache (a profiling case, not the benchmark workload)")
     if world == 1 and not args.no_reference_gpu:
-        line["reference_gpu"] = reference_gpu_layer(batch, args.steps, ms_per_step, local_rank,
-                                                    step.run(t))
+        line["reference_gpu"] = guarded(reference_gpu_layer, batch, args.steps, ms_per_step,
+                                        local_rank, step.run(t))
     if not args.no_cpu_baseline and world == 1:  # rank 0 at N=1 only
-        line["cpu_baseline"] = cpu_baseline(batch, budget_s=args.cpu_seconds)
+        line["cpu_baseline"] = guarded(cpu_baseline, batch, budget_s=args.cpu_seconds)
     if world == 1 and not args.no_rows:
         del step, t, batch
-        torch.cuda.empty_cache()
+        guarded(torch.cuda.empty_cache)
         line["rows"] = run_rows(args, local_rank)
     return line
 
@@ -689,6 +696,15 @@ def _compact(line: dict) -> dict:
     return {k: line[k] for k in keep if k in line}
 
 
+def guarded(fn, *args, **kw):
+    """fn(*args, **kw), or {"error": ...} if it raises: an optional leg of the
+    bench never keeps the headline line from being printed."""
+    try:
+        return fn(*args, **kw)
+    except Exception as e:  # noqa: BLE001 -- recorded in the JSON line
+        return {"error": f"{type(e).__name__}: {e}"[:500]}
+
+
 def run_rows(args, local_rank: int) -> dict:
     """Each row in turn on this GPU, its memory freed before the next; a row
     that fails records its error and the others still run."""
@@ -696,13 +712,13 @@ def run_rows(args, local_rank: int) -> dict:
     for name, fn in (("c3_decode_step", row_c3_step), ("decode_attention", run_attention),
                      ("prefill_attention", run_prefill), ("sampler", run_sample),
                      ("c5_long_prefill", row_c5)):
-        try:
+        def one():
             line = fn(args, 0, 1, local_rank, as_row=True)
-            rows[name] = _compact(line) if line is not None else None
-        except Exception as e:
-            rows[name] = {"error": f"{type(e).__name__}: {e}"}
-        torch.cuda.synchronize()
-        torch.cuda.empty_cache()
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+            return _compact(line) if line is not None else None
+
+        rows[name] = guarded(one)
     return rows
 
 
