@@ -198,22 +198,25 @@ def test_persistent_schedule_matches_one_cta_per_item(lens):
         assert counter.tolist() == [0, 0]
 
 
+@pytest.mark.parametrize("step", [128, 64, 32])
 @pytest.mark.parametrize("scale", [1.0, 3.0])
-def test_large_scores_growing_across_blocks(scale):
+def test_large_scores_growing_across_blocks(scale, step):
     """Scores whose row max grows by far more than 2^8 (and 2^32) from one
-    128-key block to the next: the one-pass softmax's lazy rescale and its
-    recompute path for rows whose probabilities would overflow."""
+    run of `step` keys to the next: from block to block (128), from the first
+    64 keys of a block to the last 64 (64), and from quarter to quarter (32).
+    Covers the one-pass softmax's lazy rescale and its recompute path for
+    rows whose probabilities would overflow, in either half of a block."""
     lens = [700, 300]
-    q, k, v, cu = _packed(lens, 8, 4, 128, torch.bfloat16, seed=int(scale * 10) + 70)
-    # every 128-key block's keys larger than the block before's
+    q, k, v, cu = _packed(lens, 8, 4, 128, torch.bfloat16, seed=int(scale * 10) + 70 + step)
+    # every run of `step` keys larger than the run before
     pos = torch.cat([torch.arange(n) for n in lens])
-    k = (k.float() * (1.0 + (pos // 128).float()).view(-1, 1, 1)).to(torch.bfloat16)
+    k = (k.float() * (1.0 + (pos // step).float() * (step / 128)).view(-1, 1, 1)).to(torch.bfloat16)
     expected = oracle.varlen_attention(q, k, v, cu, cu, True, softmax_scale=scale)
     out = tsb.flash_attn_varlen_func(q.to(DEV), k.to(DEV), v.to(DEV), cu.to(DEV), cu.to(DEV),
                                      max(lens), max(lens), True, softmax_scale=scale)
     tsb.check_errors()
     assert torch.isfinite(out).all()
-    assert_close(out, expected, f"growing scores scale={scale}", min_exact=0.0)
+    assert_close(out, expected, f"growing scores scale={scale} step={step}", min_exact=0.0)
 
 
 def test_cuda_graph_replays():
