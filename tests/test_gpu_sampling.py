@@ -103,6 +103,26 @@ def test_qwen3_vocab_decode_batch():
     assert n <= 8, f"{n} boundary rows out of 256"
 
 
+@pytest.mark.parametrize("scale", [1.0, 4.0])
+def test_candidate_sets_on_both_sides_of_the_one_pass_limit(scale):
+    """Rows whose filtered head (everything at or above the level-1 digit of
+    the top-k cut, or of the top-p cut without top-k) holds from a few to
+    thousands of elements, so the kernel takes its one-pass path on some and
+    its select path on others; the tokens must match the oracle either way."""
+    g = torch.Generator().manual_seed(int(scale * 7) + 40)
+    B, V = 48, 151936
+    logits = (torch.randn(B, V, generator=g) * scale).to(torch.bfloat16)
+    temperature = torch.tensor([0.7, 1.0, 1.3] * 16)
+    top_k = torch.tensor([20, 1500, 2000, 2048, 2049, 2600, 0, 0] * 6)
+    top_p = torch.tensor([1.0, 0.95, 1.0, 0.9, 1.0, 0.8, 0.5, 0.99] * 6)
+    uniforms = oracle.uniforms_from_seeds(torch.randint(0, 2 ** 62, (B,), generator=g).tolist(),
+                                          [7] * B)
+    args = (logits, temperature, top_k, top_p, uniforms)
+    expected = oracle.sample_tokens(*args)
+    out = tsb.sample_tokens(*(t.to(DEV) for t in args))
+    _check_against(out, expected, args, f"one-pass limit scale={scale}")
+
+
 def test_strided_and_unaligned_rows():
     """Rows of a wider buffer (16-byte aligned row stride, vector loads) and
     rows at an odd bf16 stride (scalar loads) give the same tokens."""

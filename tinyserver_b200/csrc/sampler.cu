@@ -91,6 +91,19 @@ struct Crossing {
 // Candidates of one select: the elements under a digit prefix, at most
 // kCand of them across the cluster.
 constexpr int kCand = 512;
+// Candidates of the one-pass path: every element whose level-1 digit is at or
+// above the boundary digit, at most kUni of them across the cluster.  Rank 0
+// sorts them as (u64 key, u64 mass) pairs in its own slice's shared memory,
+// which the launcher sizes to at least kUni * 16 bytes.  The path is taken up
+// to kUniTake candidates: a larger sort by one CTA costs more than the
+// cluster-wide selects (on Qwen3's vocabulary, 2048 candidates took ~8%
+// longer per row than top-k and a pick by selects).
+constexpr int kUni = 2048;
+#ifndef QF_SAMPLE_UNI_TAKE
+#define QF_SAMPLE_UNI_TAKE 512
+#endif
+constexpr int kUniTake = QF_SAMPLE_UNI_TAKE;
+static_assert(kUniTake <= kUni, "one-pass candidates fit the buffers");
 
 struct SampleShared {
     union {
@@ -107,6 +120,10 @@ struct SampleShared {
             u64 key[kCand];         // all of the cluster's: (order desc, index asc) as a u64
             u64 w[kCand];           // and masses
         } c;
+        struct {  // the one-pass path: this CTA's elements at or above the boundary digit
+            float s[kUni];
+            uint32_t idx[kUni];
+        } x;
     } u;
     // A level's histogram summed over the cluster: this CTA's range of bins,
     // and every 32-bin group's totals (pushed here by the group's owner).
@@ -514,10 +531,12 @@ __device__ Selected select_candidates(const cg::cluster_group& cl, SampleShared&
     return out;
 }
 
+// `known`: the level-1 crossing of this same threshold, when the caller has it.
 __device__ Selected select_rank(const cg::cluster_group& cl, SampleShared& sm, const float* sv,
-                                int n, int64_t base, float m, bool by_mass, u64 tau, int& nsel) {
+                                int n, int64_t base, float m, bool by_mass, u64 tau, int& nsel,
+                                const Crossing* known = nullptr) {
     Selected out{};
-    const Crossing f1 = search_all(cl, sm, 0, by_mass, tau, 0, 0);
+    const Crossing f1 = known ? *known : search_all(cl, sm, 0, by_mass, tau, 0, 0);
     if (!f1.found) return out;
     const uint32_t p1 = (uint32_t)f1.digit;
     if (f1.cnt <= (u64)kCand)
@@ -576,6 +595,156 @@ __device__ int nth_with_key(SampleShared& sm, const float* sv, int n, uint32_t k
     }
     __syncthreads();
     return sm.owner;
+}
+
+// First position r of the nondecreasing incl[0, n) with incl[r] >= tau, or -1.
+// Whole CTA.
+__device__ int first_reaching(SampleShared& sm, const u64* incl, int n, u64 tau) {
+    if (threadIdx.x == 0) sm.owner = -1;
+    __syncthreads();
+    for (int r = threadIdx.x; r < n; r += kThreads)
+        if (incl[r] >= tau && (r == 0 || incl[r - 1] < tau)) sm.owner = r;  // one such r
+    __syncthreads();
+    const int r = sm.owner;
+    __syncthreads();
+    return r;
+}
+
+// The one-pass path.  Every rank that top-k, top-p and the pick can land on
+// has its level-1 digit >= dstar, and ncand <= kUni elements of the row do
+// (the caller checked).  Every CTA compacts its own; rank 0 gathers them,
+// sorts them by (s desc, index asc) -- the rank order -- sums their masses in
+// that order and reads the three thresholds off the sums.  These are the same
+// integers the select path computes (the top-k cut's inclusive mass, the first
+// rank whose inclusive mass reaches tau), so the token is the same.  Called by
+// every CTA of the cluster; returns with all of them past the final barrier.
+__device__ void sample_unified(const cg::cluster_group& cl, SampleShared& sm, float* sv, int n,
+                               int64_t base, float m, uint32_t dstar, bool use_k, u64 k_eff,
+                               bool use_p, float top_p, u64 z_all, float u, int64_t* out) {
+    const int rank = (int)cl.block_rank();
+    if (threadIdx.x == 0) sm.cand_n[0] = 0;
+    __syncthreads();
+    auto take = [&](float s, int i) {
+        if ((order_key(s) >> 21) >= dstar) {
+            const uint32_t slot = atomicAdd(&sm.cand_n[0], 1u);
+            if (slot < kUni) {  // always: this CTA's share of at most kUni
+                sm.u.x.s[slot] = s;
+                sm.u.x.idx[slot] = (uint32_t)(base + i);
+            }
+        }
+    };
+    const int n4 = n >> 2;
+    const float4* s4 = reinterpret_cast<const float4*>(sv);
+    for (int q = threadIdx.x; q < n4; q += kThreads) {
+        const float4 v = s4[q];
+        take(v.x, 4 * q);
+        take(v.y, 4 * q + 1);
+        take(v.z, 4 * q + 2);
+        take(v.w, 4 * q + 3);
+    }
+    for (int i = (n4 << 2) + (int)threadIdx.x; i < n; i += kThreads) take(sv[i], i);
+    cl.sync();  // every CTA's candidates are in place
+    if (rank == 0) {
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        if (threadIdx.x < 32) {
+            uint32_t c = 0;
+            if (lane < kClusterCtas)
+                c = min(cl.map_shared_rank(&sm, lane)->cand_n[0], (uint32_t)kUni);
+            uint32_t incl = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += x;
+            }
+            if (lane < kClusterCtas) sm.cand_pre[lane + 1] = incl;
+            if (lane == 0) sm.cand_pre[0] = 0;
+        }
+        __syncthreads();
+        const int total = (int)min(sm.cand_pre[kClusterCtas], (uint32_t)kUni);
+        int P = 1;
+        while (P < total) P <<= 1;
+        // (key, mass) pairs over this CTA's slice, which it no longer needs
+        u64* yk = reinterpret_cast<u64*>(sv);
+        u64* yw = yk + kUni;
+        for (int t = threadIdx.x; t < P; t += kThreads) {
+            u64 key = ~0ull, w = 0;  // padding sorts last
+            if (t < total) {
+                int q = 0;
+                while (q + 1 < kClusterCtas && (int)sm.cand_pre[q + 1] <= t) ++q;
+                const SampleShared* r = cl.map_shared_rank(&sm, q);
+                const float s = r->u.x.s[t - sm.cand_pre[q]];
+                key = ((u64)(~order_key(s)) << 32) | r->u.x.idx[t - sm.cand_pre[q]];
+                w = mass_of(s, m);
+            }
+            yk[t] = key;
+            yw[t] = w;
+        }
+        __syncthreads();
+        // bitonic sort, ascending key = rank order
+        for (int k = 2; k <= P; k <<= 1) {
+            for (int j = k >> 1; j > 0; j >>= 1) {
+                for (int i = threadIdx.x; i < P; i += kThreads) {
+                    const int l = i ^ j;
+                    if (l > i) {
+                        const u64 x = yk[i], y = yk[l];
+                        if ((x > y) == ((i & k) == 0)) {
+                            yk[i] = y;
+                            yk[l] = x;
+                            const u64 t = yw[i];
+                            yw[i] = yw[l];
+                            yw[l] = t;
+                        }
+                    }
+                }
+                __syncthreads();
+            }
+        }
+        // inclusive sums of the masses in rank order: a run of `per` per thread
+        const int per = (P + kThreads - 1) / kThreads;
+        const int i0 = min(P, (int)threadIdx.x * per), i1 = min(P, i0 + per);
+        u64 run = 0;
+        for (int i = i0; i < i1; ++i) {
+            run += yw[i];
+            yw[i] = run;
+        }
+        u64 x = run;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const u64 y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) sm.red_mas[warp] = x;
+        __syncthreads();
+        if (warp == 0) {
+            u64 y = lane < kWarps ? sm.red_mas[lane] : 0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const u64 z = __shfl_up_sync(0xffffffffu, y, o);
+                if (lane >= o) y += z;
+            }
+            if (lane < kWarps) sm.red_mas[lane] = y;
+        }
+        __syncthreads();
+        const u64 off = (warp ? sm.red_mas[warp - 1] : 0) + (x - run);
+        for (int i = i0; i < i1; ++i) yw[i] += off;
+        __syncthreads();
+        // top-k: the mass of ranks < k; top-p: up to the first rank whose
+        // inclusive mass exceeds top_p * that; the pick: the first rank whose
+        // inclusive mass is >= ceil(u * the kept mass)
+        const u64 z_k = use_k ? yw[k_eff - 1] : z_all;
+        u64 z_r = z_k;
+        if (use_p) {
+            const double theta = (double)top_p * (double)z_k;
+            const u64 tau = theta < 0.0 ? 0 : (u64)floor(theta) + 1;
+            const int r = first_reaching(sm, yw, total, tau);
+            if (r >= 0 && (u64)r + 1 < k_eff) z_r = yw[r];
+        }
+        u64 tau = (u64)ceil((double)u * (double)z_r);
+        if (tau > z_r) tau = z_r;
+        const int r = first_reaching(sm, yw, total, tau);
+        if (threadIdx.x == 0) *out = r >= 0 ? (int64_t)(uint32_t)yk[r] : (int64_t)sm.row_argmax;
+    }
+    cl.sync();  // no CTA leaves while rank 0 may read its shared memory
 }
 
 template <typename T>
@@ -686,30 +855,54 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleDev a) 
     const u64 z_all = sm.z_all;
     int nsel = 0;  // candidate selects so far (picks their buffer)
 
-    // ---- top-k -------------------------------------------------------------
+    // ---- settings ----------------------------------------------------------
     const int64_t V = a.vocab;
     const int64_t k = a.top_k_i64 ? reinterpret_cast<const int64_t*>(a.top_k)[row]
                                   : (int64_t)reinterpret_cast<const int32_t*>(a.top_k)[row];
     const u64 k_eff = (k > 0 && k < V) ? (u64)k : (u64)V;
+    const float top_p = a.top_p[row];
+    const float u = a.uniforms ? a.uniforms[row]
+                               : uniform_from_hash((uint64_t)a.seeds[row], (uint64_t)a.steps[row]);
+    const bool use_k = k_eff < (u64)V, use_p = top_p < 1.0f;
+
+    // ---- one pass when the filtered head of the order is small --------------
+    // Every answer ranks at or above the top-k cut, or without top-k at or
+    // above the top-p cut (its threshold taken on the whole mass), so the
+    // level-1 digit of that cut bounds all three.
+    Crossing f0{};  // that cut's level-1 crossing, reused by its select below
+    if (use_k || use_p) {
+        u64 tau_b = k_eff;
+        if (!use_k) {
+            const double theta = (double)top_p * (double)z_all;
+            tau_b = theta < 0.0 ? 0 : (u64)floor(theta) + 1;
+        }
+        f0 = search_all(cl, sm, 0, !use_k, tau_b, 0, 0);
+        if (f0.found && f0.above_cnt + f0.cnt <= (u64)kUniTake) {
+            sample_unified(cl, sm, sv, n, base, m, (uint32_t)f0.digit, use_k, k_eff, use_p, top_p,
+                           z_all, u, a.out + row);
+            return;
+        }
+    }
+
+    // ---- top-k -------------------------------------------------------------
     u64 z_k = z_all;
-    if (k_eff < (u64)V) {
-        const Selected c = select_rank(cl, sm, sv, n, base, m, false, k_eff, nsel);
+    if (use_k) {
+        const Selected c = select_rank(cl, sm, sv, n, base, m, false, k_eff, nsel, &f0);
         if (c.found) z_k = c.incl_mas;
     }
 
     // ---- top-p -------------------------------------------------------------
-    const float top_p = a.top_p[row];
     u64 z_r = z_k;
-    if (top_p < 1.0f) {
+    if (use_p) {
         const double theta = (double)top_p * (double)z_k;
         const u64 tau = theta < 0.0 ? 0 : (u64)floor(theta) + 1;
-        const Selected c = select_rank(cl, sm, sv, n, base, m, true, tau, nsel);
+        // without top-k, z_k is z_all and tau the threshold f0 was found for
+        const Selected c =
+            select_rank(cl, sm, sv, n, base, m, true, tau, nsel, use_k ? nullptr : &f0);
         if (c.found && c.incl_cnt < k_eff) z_r = c.incl_mas;
     }
 
     // ---- the pick ----------------------------------------------------------
-    const float u = a.uniforms ? a.uniforms[row]
-                               : uniform_from_hash((uint64_t)a.seeds[row], (uint64_t)a.steps[row]);
     u64 tau = (u64)ceil((double)u * (double)z_r);
     if (tau > z_r) tau = z_r;
     const Selected pick = select_rank(cl, sm, sv, n, base, m, true, tau, nsel);
@@ -771,7 +964,8 @@ int launch_sample(const SampleDev& a, int64_t batch, cudaStream_t stream) {
         if (e != cudaSuccess) return launch_failed(e);
         max_dyn.store(dyn, std::memory_order_relaxed);
     }
-    const size_t smem = (size_t)a.slice * sizeof(float);
+    // the slice as fp32, and room for the one-pass path's sorted pairs
+    const size_t smem = std::max((size_t)a.slice * sizeof(float), (size_t)kUni * 2 * sizeof(u64));
     if ((int64_t)smem > max_dyn.load(std::memory_order_relaxed)) return QF_ERR_UNSUPPORTED;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(batch * kClusterCtas));
