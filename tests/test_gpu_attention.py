@@ -127,6 +127,40 @@ def test_block_outside_the_cache_is_flagged_not_read():
         tsb.check_errors()
 
 
+@pytest.mark.parametrize("split", [True, False])
+@pytest.mark.parametrize("bsz", [8, 16, 32])
+def test_16bit_pages_with_poisoned_tails(bsz, split):
+    """The 16-bit kernel copies each 16-key tile with cp.async, keys past the
+    sequence zero-filled, at block sizes below, equal to and above the tile.
+    Slots past each sequence's end hold NaN: none may reach the output,
+    through S or through P V."""
+    lens = [1, 5, 16, 17, 40, 300, 1029, 2048, 3000]
+    q, kc, vc, bt, sl = _paged_inputs(lens, 32, 8, 128, bsz, torch.bfloat16, seed=bsz + 77)
+    for s, n in enumerate(lens):
+        if n % bsz:
+            last = int(bt[s, (n - 1) // bsz])
+            kc[last, :, n % bsz:, :] = float("nan")
+            vc[last, :, n % bsz:, :] = float("nan")
+    expected = oracle.paged_attention_decode(q, kc, vc, bt, bsz, sl)
+    out = tsb.paged_attention_forward(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), bsz,
+                                      sl.to(DEV), split=split)
+    tsb.check_errors()
+    assert torch.isfinite(out).all()
+    _check(out, expected, f"block {bsz} split={split}")
+
+
+def test_16bit_block_outside_the_cache_is_flagged_not_read():
+    """A bad block index in the middle of a 16-bit sequence: flagged, its
+    keys zero-filled and masked, the output finite."""
+    q, kc, vc, bt, sl = _paged_inputs([200], 32, 8, 128, 16, torch.bfloat16, seed=5)
+    bt[0, 3] = kc.shape[0] + 1000
+    out = tsb.paged_attention_forward(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), 16,
+                                      sl.to(DEV))
+    with pytest.raises(IndexError, match="block index"):
+        tsb.check_errors()
+    assert torch.isfinite(out).all()
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("split", [True, False])
 def test_length_beyond_the_block_table_is_cut_and_flagged(dtype, split):
