@@ -336,9 +336,26 @@ typedef struct {
     const float* uniforms;
     const int64_t* seeds; const int64_t* steps;
     int64_t* out;
+    /* Scratch for the batch-wide path, at least qf_sample_workspace_bytes(batch)
+     * bytes, 256-byte aligned; its contents need no initialisation.  Calls
+     * that may overlap on the GPU need workspaces of their own.  NULL: every
+     * row runs on the per-row cluster kernel. */
+    void* workspace; int64_t workspace_bytes;
+    /* QF_SAMPLE_PATH_AUTO: the batch-wide path when a workspace is given and
+     * the batch is large enough; QF_SAMPLE_PATH_CLUSTER: the per-row cluster
+     * kernel; QF_SAMPLE_PATH_WIDE: the batch-wide path (needs the workspace,
+     * at most 65535 rows).  Every path returns the same tokens. */
+    int path;
 } qf_sample_args;
 
+enum { QF_SAMPLE_PATH_AUTO = 0, QF_SAMPLE_PATH_CLUSTER = 1, QF_SAMPLE_PATH_WIDE = 2 };
+
 int qf_sample_tokens(const qf_sample_args* args, cudaStream_t stream);
+
+/* Bytes of workspace the batch-wide sampling path needs for `batch` rows
+ * (~66 KB a row, whatever the vocabulary).  No counterpart in the reference,
+ * whose sort allocates its own temporaries. */
+int64_t qf_sample_workspace_bytes(int64_t batch);
 
 /* sizeof(qf_sample_args) as compiled into the library. */
 size_t qf_sample_args_size(void);

@@ -85,26 +85,70 @@ def _random_case(B, V, dtype, seed, scale=3.0):
     return logits, temperature, top_k, top_p, uniforms
 
 
+PATHS = ["cluster", "wide"]
+
+
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("V", [1, 2, 7, 100, 4099, 32000])
-def test_random_rows_against_oracle(dtype, V):
+def test_random_rows_against_oracle(dtype, V, path):
     args = _random_case(24, V, dtype, seed=V)
     expected = oracle.sample_tokens(*args)
-    out = tsb.sample_tokens(*(t.to(DEV) for t in args))
-    _check_against(out, expected, args, f"{dtype} V={V}")
+    out = tsb.sample_tokens(*(t.to(DEV) for t in args), path=path)
+    _check_against(out, expected, args, f"{dtype} V={V} {path}")
 
 
-def test_qwen3_vocab_decode_batch():
+@pytest.mark.parametrize("path", PATHS)
+def test_qwen3_vocab_decode_batch(path):
     """A c3-sized decode batch: 256 rows of Qwen3's 151936-token vocabulary."""
     args = _random_case(256, 151936, torch.bfloat16, seed=3, scale=4.0)
     expected = oracle.sample_tokens(*args)
-    out = tsb.sample_tokens(*(t.to(DEV) for t in args))
-    n = _check_against(out, expected, args, "qwen3 vocab")
+    out = tsb.sample_tokens(*(t.to(DEV) for t in args), path=path)
+    n = _check_against(out, expected, args, f"qwen3 vocab {path}")
     assert n <= 8, f"{n} boundary rows out of 256"
 
 
+def _mixed_rows(B, V, seed, scale, dtype=torch.bfloat16):
+    """Rows for both sampling paths: greedy rows, top-k cuts from 1 to far
+    past the batch-wide path's candidate buffer, top-p and plain picks over
+    peaked and flat logits, uniforms from 0 to just below 1."""
+    g = torch.Generator().manual_seed(seed)
+    logits = (torch.randn(B, V, generator=g) * scale).to(dtype)
+    pick = lambda vals: torch.tensor(vals)[torch.randint(0, len(vals), (B,), generator=g)]  # noqa
+    temperature = pick([0.0, 0.6, 1.0, 1.3, 4.0])
+    top_k = pick([0, 0, 0, 1, 50, 2048, 4096, 4097, 6000, 30000, V + 3])
+    top_p = pick([1.0, 1.0, 0.5, 0.9, 0.95, 0.999, 0.0])
+    uniforms = torch.rand(B, generator=g)
+    uniforms[::7] = 1 - 2 ** -24
+    uniforms[::11] = 0.0
+    return logits, temperature, top_k, top_p, uniforms
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("B,V,scale", [(64, 151936, 4.0), (300, 151936, 0.5), (48, 4099, 1.0),
+                                       (40, 32000, 8.0), (33, 37, 2.0)])
+def test_wide_path_gives_the_cluster_kernels_tokens(B, V, scale, dtype):
+    """The batch-wide passes compute the same integers as the per-row cluster
+    kernel, so the tokens are identical on every row, boundary rows included;
+    rows the batch-wide passes leave (candidate sets past the buffer, large
+    top-k) go to the cluster kernel inside the same call."""
+    args = [t.to(DEV) for t in _mixed_rows(B, V, seed=B + V, scale=scale, dtype=dtype)]
+    wide = tsb.sample_tokens(*args, path="wide")
+    cluster = tsb.sample_tokens(*args, path="cluster")
+    assert torch.equal(wide, cluster), (wide != cluster).nonzero().flatten().tolist()[:8]
+    assert torch.equal(tsb.sample_tokens(*args, path="wide"), wide)  # workspace reuse
+
+
+def test_wide_path_against_oracle_with_rows_left_to_the_cluster_kernel():
+    args = _mixed_rows(96, 151936, seed=5, scale=0.5)
+    expected = oracle.sample_tokens(*args)
+    out = tsb.sample_tokens(*(t.to(DEV) for t in args), path="wide")
+    _check_against(out, expected, args, "wide, mixed rows")
+
+
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("scale", [1.0, 4.0])
-def test_candidate_sets_on_both_sides_of_the_one_pass_limit(scale):
+def test_candidate_sets_on_both_sides_of_the_one_pass_limit(scale, path):
     """Rows whose filtered head (everything at or above the level-1 digit of
     the top-k cut, or of the top-p cut without top-k) holds from a few to
     thousands of elements, so the kernel takes its one-pass path on some and
@@ -119,8 +163,8 @@ def test_candidate_sets_on_both_sides_of_the_one_pass_limit(scale):
                                           [7] * B)
     args = (logits, temperature, top_k, top_p, uniforms)
     expected = oracle.sample_tokens(*args)
-    out = tsb.sample_tokens(*(t.to(DEV) for t in args))
-    _check_against(out, expected, args, f"one-pass limit scale={scale}")
+    out = tsb.sample_tokens(*(t.to(DEV) for t in args), path=path)
+    _check_against(out, expected, args, f"one-pass limit scale={scale} {path}")
 
 
 def test_strided_and_unaligned_rows():
@@ -138,7 +182,8 @@ def test_strided_and_unaligned_rows():
         _check_against(out, expected, args, f"row stride {width}")
 
 
-def test_ties_follow_index_order():
+@pytest.mark.parametrize("path", PATHS)
+def test_ties_follow_index_order(path):
     """Long runs of equal logits: the stable sort puts equal values in index
     order, which decides both the top-k cut and the picked token."""
     g = torch.Generator().manual_seed(5)
@@ -150,17 +195,18 @@ def test_ties_follow_index_order():
     uniforms = torch.linspace(0, 1 - 2 ** -24, B)
     args = (logits, temperature, top_k, top_p, uniforms)
     expected = oracle.sample_tokens(*args)
-    out = tsb.sample_tokens(*(t.to(DEV) for t in args))
-    _check_against(out, expected, args, "ties")
+    out = tsb.sample_tokens(*(t.to(DEV) for t in args), path=path)
+    _check_against(out, expected, args, f"ties {path}")
 
 
-def test_seeded_variant_equals_explicit_uniforms():
+@pytest.mark.parametrize("path", PATHS)
+def test_seeded_variant_equals_explicit_uniforms(path):
     args = _random_case(32, 5000, torch.bfloat16, seed=21)
     seeds = list(range(1000, 1032))
     steps = [3 * i for i in range(32)]
     u = tsb.uniforms_from_seeds(seeds, steps)
-    a = tsb.sample_tokens(*(t.to(DEV) for t in args[:4]), u)
-    b = tsb.sample_tokens_seeded(*(t.to(DEV) for t in args[:4]), seeds, steps)
+    a = tsb.sample_tokens(*(t.to(DEV) for t in args[:4]), u, path=path)
+    b = tsb.sample_tokens_seeded(*(t.to(DEV) for t in args[:4]), seeds, steps, path=path)
     assert torch.equal(a, b)
     assert torch.equal(u.cpu(), oracle.uniforms_from_seeds(seeds, steps))
 

@@ -108,6 +108,8 @@ class SampleArgs(ctypes.Structure):
         ("uniforms", c_vp),
         ("seeds", c_vp), ("steps", c_vp),
         ("out", c_vp),
+        ("workspace", c_vp), ("workspace_bytes", c_i64),
+        ("path", c_int),
     ]
 
 
@@ -136,6 +138,7 @@ SIGNATURES: dict[str, list] = {
     "qf_varlen_attention": [ctypes.POINTER(VarlenAttentionArgs), c_vp],
     "qf_varlen_attention_args_size": [],
     "qf_sample_tokens": [ctypes.POINTER(SampleArgs), c_vp],
+    "qf_sample_workspace_bytes": [c_i64],
     "qf_sample_args_size": [],
     "qf_uniforms_from_seeds": [c_vp, c_vp, c_i64, c_vp, c_vp],
     "qf_read_status": [c_vp, ctypes.POINTER(ctypes.c_int32), c_int, c_vp],
@@ -147,6 +150,7 @@ RESTYPES = {"qf_last_cuda_error": ctypes.c_char_p, "qf_version": ctypes.c_char_p
             "qf_paged_attention_args_size": ctypes.c_size_t,
             "qf_paged_attention_workspace_bytes": ctypes.c_size_t,
             "qf_paged_attention_noalloc_capacity": ctypes.c_size_t,
+            "qf_sample_workspace_bytes": c_i64,
             "qf_varlen_attention_args_size": ctypes.c_size_t,
             "qf_sample_args_size": ctypes.c_size_t}
 

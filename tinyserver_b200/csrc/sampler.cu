@@ -34,7 +34,7 @@
 // row in shared memory as fp32 s, so the row is read from HBM once.
 #include <cooperative_groups.h>
 
-#include "qf_common.cuh"
+#include "qf_sample.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -46,6 +46,9 @@ namespace {
 #endif
 #ifndef QF_SAMPLE_LOADS
 #define QF_SAMPLE_LOADS 5  // 16-byte loads in flight per thread: a whole slice in one batch
+#endif
+#ifndef QF_SAMPLE_WIDE_MIN_ROWS
+#define QF_SAMPLE_WIDE_MIN_ROWS 128  // auto: the batch-wide path from this many rows on
 #endif
 #ifndef QF_SAMPLE_PREFETCH
 #define QF_SAMPLE_PREFETCH 1  // prefetch into L2 the slice the next wave of clusters reads
@@ -59,9 +62,7 @@ constexpr int kOwn = kBins / kClusterCtas;      // combined bins each CTA holds
 constexpr int kGroup = 32;                      // bins per group (one warp's scan)
 constexpr int kGroups = kBins / kGroup;         // 64: two per lane of the scanning warp
 constexpr int kOwnGroups = kOwn / kGroup;
-constexpr float kMassScale = 1099511627776.0f;  // 2^40
 static_assert(kOwn <= kThreads && kOwn % kGroup == 0 && kGroups == 64, "cluster size 4..64");
-using u64 = unsigned long long;
 
 struct SampleDev {
     const char* logits;
@@ -78,6 +79,10 @@ struct SampleDev {
     const int64_t* seeds;
     const int64_t* steps;
     int64_t* out;
+    // optional: the rows to sample, rows[0 .. *nrows) (device), one cluster
+    // each; clusters past *nrows exit at once.  NULL: cluster c samples row c.
+    const uint32_t* rows;
+    const uint32_t* nrows;
 };
 
 // The crossing found by a descending scan: its digit, the cumulative weight
@@ -153,30 +158,6 @@ struct SampleShared {
     } cres;
 };
 
-__device__ __forceinline__ uint32_t order_key(float s) {
-    const uint32_t b = __float_as_uint(s);
-    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-}
-
-__device__ __forceinline__ u64 mass_of(float s, float m) {
-    return __float2ull_rn(expf(s - m) * kMassScale);
-}
-
-__device__ __forceinline__ bool better(float s, uint32_t i, float t, uint32_t j) {
-    return s > t || (s == t && i < j);
-}
-
-// splitmix64 of (seed, step), top 53 bits as a double in [0, 1), clamped to
-// the largest float32 below 1 -- uniform_from_hash, determinism.py:30-51.
-__device__ __forceinline__ float uniform_from_hash(uint64_t seed, uint64_t step) {
-    uint64_t x = seed * 0x9E3779B97F4A7C15ull + step;
-    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
-    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
-    x ^= x >> 31;
-    const double u = fmin((double)(x >> 11) * 0x1p-53, 1.0 - 0x1p-24);
-    return __double2float_rn(u);
-}
-
 template <typename F>
 __device__ __forceinline__ void for_each_s(const float* sv, int n, F&& f) {
     const int n4 = n >> 2;
@@ -189,12 +170,6 @@ __device__ __forceinline__ void for_each_s(const float* sv, int n, F&& f) {
         f(v.w);
     }
     for (int i = (n4 << 2) + (int)threadIdx.x; i < n; i += kThreads) f(sv[i]);
-}
-
-template <typename T>
-__device__ __forceinline__ float scaled(T x, float tc) {
-    const float s = __fdiv_rn(Dt<T>::to_f(x), tc);
-    return s == 0.0f ? 0.0f : s;  // -0 ranks with +0, as in the sort
 }
 
 // Load this CTA's slice, write s to shared memory, return the thread's best
@@ -753,7 +728,12 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleDev a) 
     __shared__ SampleShared sm;
     const cg::cluster_group cl = cg::this_cluster();
     const int rank = (int)cl.block_rank();
-    const int64_t row = blockIdx.x / kClusterCtas;
+    int64_t row = blockIdx.x / kClusterCtas;
+    if (a.rows) {  // every CTA of a cluster reads the same count and entry
+        if ((uint32_t)row >= *a.nrows) return;
+        row = a.rows[row];
+        if (row >= (int64_t)(gridDim.x / kClusterCtas)) return;  // not a row of the batch
+    }
     const int64_t base = (int64_t)rank * a.slice;
     const int64_t left = a.vocab - base;
     const int n = left <= 0 ? 0 : (left < a.slice ? (int)left : a.slice);
@@ -993,7 +973,7 @@ int launch_sample(const SampleDev& a, int64_t batch, cudaStream_t stream) {
         wave_key.store(key, std::memory_order_relaxed);
     }
     SampleDev b = a;
-    b.ahead = wave.load(std::memory_order_relaxed);
+    b.ahead = a.rows ? 0 : wave.load(std::memory_order_relaxed);
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, b);
     return e == cudaSuccess ? QF_OK : launch_failed(e);
 }
@@ -1027,11 +1007,53 @@ extern "C" int qf_sample_tokens(const qf_sample_args* p, cudaStream_t stream) {
     a.seeds = g.seeds;
     a.steps = g.steps;
     a.out = g.out;
+    // the batch-wide passes, when asked for or when the batch is large enough
+    // to keep the GPU busy with them; rows they leave go to the cluster kernel
+    const bool ws_ok = g.workspace &&
+                       g.workspace_bytes >= qf::sample_wide_workspace_bytes(g.batch) &&
+                       (reinterpret_cast<uintptr_t>(g.workspace) & 255u) == 0;
+    bool wide = false;
+    switch (g.path) {
+    case QF_SAMPLE_PATH_AUTO:
+        wide = ws_ok && g.batch >= QF_SAMPLE_WIDE_MIN_ROWS && g.batch <= 65535;
+        break;
+    case QF_SAMPLE_PATH_CLUSTER: break;
+    case QF_SAMPLE_PATH_WIDE:
+        if (!ws_ok) return QF_ERR_INVALID;
+        if (g.batch > 65535) return QF_ERR_UNSUPPORTED;
+        wide = true;
+        break;
+    default: return QF_ERR_INVALID;
+    }
+    if (wide) {
+        qf::WideArgs w{};
+        w.logits = g.logits;
+        w.row_stride = g.logits_row_stride;
+        w.batch = g.batch;
+        w.vocab = g.vocab;
+        w.dtype = g.dtype;
+        w.vec = a.vec;
+        w.temperature = g.temperature;
+        w.top_k = g.top_k;
+        w.top_k_i64 = a.top_k_i64;
+        w.top_p = g.top_p;
+        w.uniforms = g.uniforms;
+        w.seeds = g.seeds;
+        w.steps = g.steps;
+        w.out = g.out;
+        w.workspace = g.workspace;
+        const int rc = qf::sample_wide_passes(w, stream, &a.rows, &a.nrows);
+        if (rc != QF_OK) return rc;
+    }
     switch (g.dtype) {
     case QF_F32: return qf::launch_sample<float>(a, g.batch, stream);
     case QF_F16: return qf::launch_sample<__half>(a, g.batch, stream);
     default: return qf::launch_sample<__nv_bfloat16>(a, g.batch, stream);
     }
+}
+
+extern "C" int64_t qf_sample_workspace_bytes(int64_t batch) {
+    return batch <= 0 ? 0 : qf::sample_wide_workspace_bytes(batch);
 }
 
 extern "C" int qf_uniforms_from_seeds(const int64_t* seeds, const int64_t* steps, int64_t n,

@@ -44,9 +44,19 @@ def _as_u64_bits(values: Sequence[int] | torch.Tensor, device: torch.device) -> 
     return torch.tensor(wrapped, dtype=torch.int64, device=device)
 
 
+# Which kernels sample a batch: "cluster" runs each row on a cluster of CTAs
+# (one row's ~10 steps back to back, ~37 rows in flight on a B200); "wide"
+# runs every step as one launch over all rows, with a workspace of
+# qf_sample_workspace_bytes(batch), and hands the rows it cannot finish to the
+# cluster kernel; "auto" takes "wide" from WIDE_MIN_ROWS rows on.  Every path
+# gives the same tokens.
+_PATHS = {"auto": 0, "cluster": 1, "wide": 2}
+WIDE_MIN_ROWS, WIDE_MAX_ROWS = 128, 65535
+
+
 def _launch(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
             top_p: torch.Tensor, uniforms: torch.Tensor | None, seeds: torch.Tensor | None,
-            steps: torch.Tensor | None, what: str) -> torch.Tensor:
+            steps: torch.Tensor | None, what: str, path: str = "auto") -> torch.Tensor:
     if logits.ndim != 2:
         raise ValueError(f"Expected logits shape [B, vocab_size], got {logits.ndim}D")
     batch_size, vocab_size = logits.shape
@@ -60,6 +70,8 @@ def _launch(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor
         _check_param("steps", steps, batch_size)
     if vocab_size == 0:
         raise ValueError("Expected a non-empty vocabulary")
+    if path not in _PATHS:
+        raise ValueError(f"{what}: path must be one of {sorted(_PATHS)}, got {path!r}")
     dev = require_cuda(what, logits, temperature, top_k, top_p, uniforms, seeds, steps)
     out = torch.empty(batch_size, dtype=torch.int64, device=dev)
     if batch_size == 0:
@@ -86,6 +98,12 @@ def _launch(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor
         sd, st = seeds.to(torch.int64).contiguous(), steps.to(torch.int64).contiguous()
         a.seeds, a.steps = sd.data_ptr(), st.data_ptr()
     a.out = out.data_ptr()
+    a.path = _PATHS[path]
+    ws = None
+    if path == "wide" or (path == "auto" and WIDE_MIN_ROWS <= batch_size <= WIDE_MAX_ROWS):
+        nbytes = _capi.lib().qf_sample_workspace_bytes(batch_size)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), nbytes
     with on_device(dev):
         _capi.check(_capi.lib().qf_sample_tokens(a, stream_ptr(dev)), what)
     return out
@@ -93,20 +111,25 @@ def _launch(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor
 
 @torch.inference_mode()
 def sample_tokens(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
-                  top_p: torch.Tensor, uniforms: torch.Tensor) -> torch.Tensor:
-    """Sample one token per row of ``logits`` [B, vocab] in one launch.
+                  top_p: torch.Tensor, uniforms: torch.Tensor, *,
+                  path: str = "auto") -> torch.Tensor:
+    """Sample one token per row of ``logits`` [B, vocab].
 
     temperature [B]: rows <= 0 are greedy (argmax, lowest index among equal
     maxima); top_k [B]: 0 (or >= vocab) disables; top_p [B]: 1.0 disables;
     uniforms [B] in [0, 1).  Returns [B] int64 token ids on the logits'
-    device.  Same ValueErrors as the reference for a wrong rank or shape."""
-    return _launch(logits, temperature, top_k, top_p, uniforms, None, None, "sample_tokens")
+    device.  Same ValueErrors as the reference for a wrong rank or shape.
+    ``path`` picks the kernels ("auto", "cluster", "wide"; see _PATHS); the
+    tokens do not depend on it."""
+    return _launch(logits, temperature, top_k, top_p, uniforms, None, None, "sample_tokens",
+                   path)
 
 
 @torch.inference_mode()
 def sample_tokens_seeded(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
                          top_p: torch.Tensor, seeds: torch.Tensor | Sequence[int],
-                         steps: torch.Tensor | Sequence[int]) -> torch.Tensor:
+                         steps: torch.Tensor | Sequence[int], *,
+                         path: str = "auto") -> torch.Tensor:
     """``sample_tokens(logits, ..., uniforms_from_seeds(seeds, steps))`` with
     the uniforms computed inside the sampling kernel (no separate launch, no
     host-to-device copy of the noise)."""
@@ -117,7 +140,7 @@ def sample_tokens_seeded(logits: torch.Tensor, temperature: torch.Tensor, top_k:
             f"seeds and steps must be the same length, got {len(seeds)} and {len(steps)}")
     dev = logits.device
     return _launch(logits, temperature, top_k, top_p, None, _as_u64_bits(seeds, dev),
-                   _as_u64_bits(steps, dev), "sample_tokens_seeded")
+                   _as_u64_bits(steps, dev), "sample_tokens_seeded", path)
 
 
 def uniforms_from_seeds(seeds: Sequence[int] | torch.Tensor, steps: Sequence[int] | torch.Tensor,
