@@ -718,7 +718,7 @@ def layer_config(world: int, T: int, step_bytes: int) -> dict:
 def _compact(line: dict) -> dict:
     keep = ("metric", "value", "unit", "ms_per_step", "us_per_step", "steps", "config",
             "roofline", "clocks", "e2e", "cpu_baseline", "reference_gpu", "validation",
-            "graph", "kv_store", "gpu_launches", "dtype", "e2e_note", "error")
+            "graph", "kv_store", "path", "gpu_launches", "dtype", "e2e_note", "error")
     return {k: line[k] for k in keep if k in line}
 
 
@@ -1388,9 +1388,12 @@ def run_sample(args, rank: int, world: int, local_rank: int, as_row: bool = Fals
     sets = [_sample_inputs(B, V, 1000 * rank + i, dev) for i in range(3)]
     steps = min(args.steps, 50) if as_row else args.steps
 
-    def once(i):
+    from tinyserver_b200.kernels import sampling as S
+    path = "wide" if S.WIDE_MIN_ROWS <= B <= S.WIDE_MAX_ROWS else "cluster"
+
+    def once(i, how="auto"):
         x, t, k, p, sd, st = sets[i % 3]
-        return tsb.sample_tokens_seeded(x, t, k, p, sd, st)
+        return tsb.sample_tokens_seeded(x, t, k, p, sd, st, path=how)
 
     for i in range(max(args.warmup, 3)):
         once(i)
@@ -1411,6 +1414,15 @@ def run_sample(args, rank: int, world: int, local_rank: int, as_row: bool = Fals
         torch.distributed.all_reduce(m, op=torch.distributed.ReduceOp.MAX)
         ms = float(m.item())
     per_ms = ms / steps
+    # the other path on the same batches, for comparison (not the value)
+    other = "cluster" if path == "wide" else "wide"
+    for i in range(3):
+        once(i, other)
+    torch.cuda.synchronize()
+    counter[0] = 0
+    ms_o, steps_o = event_loop(lambda: (once(counter[0], other),
+                                        counter.__setitem__(0, counter[0] + 1)), steps)
+    other_ms = ms_o / steps_o
 
     # end to end: logits from pinned host memory, tokens back to the host
     e2e = None
@@ -1478,9 +1490,15 @@ def run_sample(args, rank: int, world: int, local_rank: int, as_row: bool = Fals
         "config": {"workload": f"c3 decode step sampling: {B} rows x {V} vocab, bf16 logits"
                                + ("" if B == SAMPLE_ROWS else " (a profiling case, not the benchmark)"),
                    "rows": B, "vocab": V, "l2": "3 rotating logits buffers (233 MB > L2)"},
-        "roofline": roofline("hbm", "sample_kernel", gbs, "GB/s", ncu_traffic("sample_kernel"),
+        "roofline": roofline("hbm", "batch-wide sampler (5 kernels + cluster kernel for the rows "
+                             "it leaves)" if path == "wide" else "sample_kernel", gbs, "GB/s",
+                             None if path == "wide" else ncu_traffic("sample_kernel"),
                              bytes_per_launch=nbytes),
-        "cpu_baseline": cpu, "e2e": e2e, "reference_gpu": ref, "gpu_launches": steps,
+        "path": {"taken": path, "ms_per_step": {path: round(per_ms, 4),
+                                                other: round(other_ms, 4)},
+                 "note": "both paths give identical tokens; value is the taken path"},
+        "cpu_baseline": cpu, "e2e": e2e, "reference_gpu": ref,
+        "gpu_launches": steps * (6 if path == "wide" else 1),
         "clocks": clocks,
     }
 
