@@ -133,9 +133,10 @@ inline Layout layout(int64_t B) {
 
 __device__ __forceinline__ int depth_bin(float s, float m) {
     const float d = __fsub_rn(m, s);
-    if (d < 16.0f) return d <= 0.0f ? 0 : (int)(d * 64.0f);
-    if (d < 144.0f) return min(kDepthBins - 1, 1024 + (int)(__fsub_rn(d, 16.0f) * 8.0f));
-    return kDepthBins - 1;  // deeper, and inf / NaN
+    const bool near = d < 16.0f;  // false for NaN: the last bin
+    // d <= 0 -> 0; d >= 144, inf and NaN -> 1024 + 1023 (fminf drops the NaN)
+    const float y = near ? fmaxf(d * 64.0f, 0.0f) : fminf(__fsub_rn(d, 16.0f) * 8.0f, 1023.0f);
+    return (int)y + (near ? 0 : 1024);
 }
 
 __device__ __forceinline__ int64_t row_top_k(const WideDev& a, int64_t row) {
@@ -207,6 +208,28 @@ __device__ __forceinline__ void fetch8(const T* p, int n, int g, bool vec, Raw8<
             r.v[0] = make_uint4(w[0], w[1], w[2], w[3]);
         }
     }
+}
+
+// Whether all of a thread's kLoads groups starting at g0 are whole and can be
+// read with vector loads; then fetch them with no per-element checks.
+__device__ __forceinline__ bool groups_full(bool vec, int n, int g0) {
+    return vec && 8 * (g0 + (kLoads - 1) * kWThreads + (int)threadIdx.x + 1) <= n;
+}
+template <typename T>
+__device__ __forceinline__ void fetch_full(const T* p, int g0, Raw8<T> (&r)[kLoads]) {
+#pragma unroll
+    for (int u = 0; u < kLoads; ++u) {
+        const int e0 = 8 * (g0 + u * kWThreads + (int)threadIdx.x);
+        r[u].v[0] = ld_stream16(p + e0);
+        if constexpr (sizeof(T) == 4) r[u].v[1] = ld_stream16(p + e0 + 4);
+        r[u].cnt = 8;
+    }
+}
+template <typename T>
+__device__ __forceinline__ void fetch_any(const T* p, int n, int g0, bool vec,
+                                          Raw8<T> (&r)[kLoads]) {
+#pragma unroll
+    for (int u = 0; u < kLoads; ++u) fetch8<T>(p, n, g0 + u * kWThreads + threadIdx.x, vec, r[u]);
 }
 
 // Element j of a group: for 16-bit types its bits; as a float (exact).
@@ -302,11 +325,9 @@ __global__ void __launch_bounds__(kWThreads) wide_max_kernel(const WideDev a) {
     // larger ones)
     float best = -INFINITY;
     uint32_t best_i = kNone;
-    for (int g0 = 0; g0 < ng; g0 += kLoads * kWThreads) {
-        Raw8<T> r[kLoads];
-#pragma unroll
-        for (int u = 0; u < kLoads; ++u)
-            fetch8<T>(p, n, g0 + u * kWThreads + threadIdx.x, a.vec, r[u]);
+    // one pass over a thread's groups (inlined twice: whole groups, where
+    // every element check folds away, and the rest)
+    auto body = [&](const Raw8<T> (&r)[kLoads], int g0) {
         if constexpr (sizeof(T) == 2) {
             // the groups' largest x by packed maxima; only when it beats the
             // running best, the first element holding it (equal x, +0 and
@@ -338,6 +359,16 @@ __global__ void __launch_bounds__(kWThreads) wide_max_kernel(const WideDev a) {
                     }
                 }
             }
+        }
+    };
+    for (int g0 = 0; g0 < ng; g0 += kLoads * kWThreads) {
+        Raw8<T> r[kLoads];
+        if (groups_full(a.vec, n, g0)) {
+            fetch_full<T>(p, g0, r);
+            body(r, g0);
+        } else {
+            fetch_any<T>(p, n, g0, a.vec, r);
+            body(r, g0);
         }
     }
     if (best_i != kNone) best_i += (uint32_t)lo;
@@ -401,17 +432,16 @@ __global__ void __launch_bounds__(kWThreads) wide_hist_kernel(const WideDev a) {
         bmin = (kmax >> 3) > (uint32_t)kRawWindow ? (kmax >> 3) - kRawWindow : 0u;
         xmin = x_of_key16<T>(bmin << 3);
     }
-    for (int g0 = 0; g0 < ng; g0 += kLoads * kWThreads) {
-        Raw8<T> r[kLoads];
-#pragma unroll
-        for (int u = 0; u < kLoads; ++u)
-            fetch8<T>(p, n, g0 + u * kWThreads + threadIdx.x, a.vec, r[u]);
+    auto body = [&](const Raw8<T> (&r)[kLoads]) {
+        // 16-bit top-k rows: nothing to count when the groups' largest x is
+        // below the window
+        if constexpr (kRaw)
+            if (use_k && groups_max<T, kLoads>(r) < xmin) return;
 #pragma unroll
         for (int u = 0; u < kLoads; ++u) {
             if (use_k) {
                 if constexpr (kRaw) {
-                    Raw8<T> one[1] = {r[u]};
-                    if (groups_max<T, 1>(one) >= xmin) {
+                    {
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
                             const uint32_t k2 = keys2(word(r[u].v[0], q));
@@ -435,14 +465,21 @@ __global__ void __launch_bounds__(kWThreads) wide_hist_kernel(const WideDev a) {
                         const u64 w = mass_of(s, m);  // < 2^41
                         z += w;
                         const uint32_t wl = (uint32_t)w, wh = (uint32_t)(w >> 32);
-                        if (wl) {
-                            const uint32_t old = atomicAdd(&h_lo[d], wl);
-                            if (old + wl < old) atomicAdd(&h_hi[d], 1u);  // carry
-                        }
-                        if (wh) atomicAdd(&h_hi[d], wh);
+                        const uint32_t old = atomicAdd(&h_lo[d], wl);
+                        if (old + wl < old || wh) atomicAdd(&h_hi[d], wh + (old + wl < old));
                     }
                 }
             }
+        }
+    };
+    for (int g0 = 0; g0 < ng; g0 += kLoads * kWThreads) {
+        Raw8<T> r[kLoads];
+        if (groups_full(a.vec, n, g0)) {
+            fetch_full<T>(p, g0, r);
+            body(r);
+        } else {
+            fetch_any<T>(p, n, g0, a.vec, r);
+            body(r);
         }
     }
     __syncthreads();
@@ -715,12 +752,9 @@ __global__ void __launch_bounds__(kWThreads) wide_compact_kernel(const WideDev a
     const int lane = threadIdx.x & 31;
     // the loop bound is the same for every thread, so the warp-wide
     // reservations below always run with the whole warp
-    for (int g0 = 0; g0 < ng; g0 += kLoads * kWThreads) {
-        Raw8<T> r[kLoads];
-#pragma unroll
-        for (int u = 0; u < kLoads; ++u)
-            fetch8<T>(p, n, g0 + u * kWThreads + threadIdx.x, a.vec, r[u]);
-        u64 take = 0;  // bit 8u + j: element j of group u is a candidate
+    // bit 8u + j of the result: element j of group u is a candidate
+    auto body = [&](const Raw8<T> (&r)[kLoads]) -> u64 {
+        u64 take = 0;
         bool look = true;
         if constexpr (kRaw) look = groups_max<T, kLoads>(r) >= xlow;
 #pragma unroll
@@ -742,6 +776,18 @@ __global__ void __launch_bounds__(kWThreads) wide_compact_kernel(const WideDev a
                         take |= 1ull << (8 * u + j);
                 }
             }
+        }
+        return take;
+    };
+    for (int g0 = 0; g0 < ng; g0 += kLoads * kWThreads) {
+        Raw8<T> r[kLoads];
+        u64 take;
+        if (groups_full(a.vec, n, g0)) {
+            fetch_full<T>(p, g0, r);
+            take = body(r);
+        } else {
+            fetch_any<T>(p, n, g0, a.vec, r);
+            take = body(r);
         }
         const uint32_t mine = __popcll(take);
         uint32_t incl = mine;
