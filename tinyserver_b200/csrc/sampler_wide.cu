@@ -617,6 +617,7 @@ __global__ void __launch_bounds__(kSThreads) wide_bounds_kernel(const WideDev a)
     const float u = a.uniforms ? a.uniforms[row]
                                : uniform_from_hash((uint64_t)a.seeds[row], (uint64_t)a.steps[row]);
     const bool use_k = k_eff < (u64)V, use_p = top_p < 1.0f;
+    __shared__ __align__(16) uint32_t stage[kRawBins];  // the row's histogram
     // depth-bin ranges [r1_lo, r1_hi] and [r2_lo, r2_hi] (empty: lo > hi)
     uint32_t r1_lo = 0, r1_hi = 0, r2_lo = 1, r2_hi = 0;
     u64 base_mas = 0;
@@ -634,11 +635,14 @@ __global__ void __launch_bounds__(kSThreads) wide_bounds_kernel(const WideDev a)
     };
     if (use_k) {
         if constexpr (kRaw) {
-            // raw bins from the top: position q is bin kRawBins - 1 - q
+            // raw bins from the top: position q is bin kRawBins - 1 - q (staged
+            // through shared memory so the global reads are coalesced)
+            for (int b = threadIdx.x; b < kRawBins; b += kSThreads) stage[b] = a.cnt[row * kRawBins + b];
+            __syncthreads();
             u64 w[kRawPer];
 #pragma unroll
             for (int i = 0; i < kRawPer; ++i)
-                w[i] = a.cnt[row * kRawBins + (kRawBins - 1 - (kRawPer * (int)threadIdx.x + i))];
+                w[i] = stage[kRawBins - 1 - (kRawPer * (int)threadIdx.x + i)];
             const Cross c = block_crossing<kRawPer>(w, k_eff);
             const uint32_t t16 = c.pos == kNone ? 0 : (uint32_t)(kRawBins - 1 - c.pos) << 3;
             ok = c.pos != kNone && c.through <= (u64)kCandCap && t16 > kninf && t16 <= kpinf &&
@@ -658,10 +662,13 @@ __global__ void __launch_bounds__(kSThreads) wide_bounds_kernel(const WideDev a)
             r1_hi = c.pos;
         }
     } else {
+        u64* stage64 = reinterpret_cast<u64*>(stage);
+        for (int b = threadIdx.x; b < kDepthBins; b += kSThreads)
+            stage64[b] = a.mas[row * kDepthBins + b];
+        __syncthreads();
         u64 w[kDepthPer];
 #pragma unroll
-        for (int i = 0; i < kDepthPer; ++i)
-            w[i] = a.mas[row * kDepthBins + kDepthPer * threadIdx.x + i];
+        for (int i = 0; i < kDepthPer; ++i) w[i] = stage64[kDepthPer * threadIdx.x + i];
         const u64 z_all = h.z_all;
         u64 tau;
         if (use_p) {
