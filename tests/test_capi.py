@@ -84,6 +84,38 @@ def test_host_side_argument_checks_return_before_any_launch():
                                2, 4, 2, None, None) == _capi.QF_OK
 
 
+def test_sampler_path_and_workspace_are_checked_on_the_host():
+    """An unknown path, or the batch-wide path without a large enough,
+    256-byte aligned workspace, is refused before any device work; the
+    workspace size grows with the batch and is 0 for an empty one."""
+    lib = _capi.lib()
+    fake = 1 << 20  # never dereferenced: every call below returns on the host
+    sa = _capi.SampleArgs()
+    sa.logits, sa.logits_row_stride, sa.batch, sa.vocab, sa.dtype = fake, 16, 256, 16, 2
+    sa.temperature = sa.top_k = sa.top_p = sa.uniforms = sa.out = fake
+    sa.top_k_type = _capi.QF_I64
+    sa.path = 7
+    assert lib.qf_sample_tokens(ctypes.byref(sa), None) == _capi.QF_ERR_INVALID
+    sa.path = 2  # batch-wide, no workspace
+    assert lib.qf_sample_tokens(ctypes.byref(sa), None) == _capi.QF_ERR_INVALID
+    need = lib.qf_sample_workspace_bytes(256)
+    sa.workspace, sa.workspace_bytes = fake, need - 1
+    assert lib.qf_sample_tokens(ctypes.byref(sa), None) == _capi.QF_ERR_INVALID
+    sa.workspace, sa.workspace_bytes = fake + 16, need  # misaligned
+    assert lib.qf_sample_tokens(ctypes.byref(sa), None) == _capi.QF_ERR_INVALID
+    assert lib.qf_sample_workspace_bytes(0) == 0
+    assert 0 < lib.qf_sample_workspace_bytes(1) < need < 2 * lib.qf_sample_workspace_bytes(128) + 4096
+
+
+def test_sampler_path_name_is_checked():
+    import torch
+    from tinyserver_b200.kernels import sampling
+    z = torch.zeros(2, 4)
+    with pytest.raises(ValueError, match="path must be one of"):
+        sampling._launch(z, torch.ones(2), torch.zeros(2, dtype=torch.int64), torch.ones(2),
+                         torch.zeros(2), None, None, "sample_tokens", "fastest")
+
+
 def test_ensure_built_is_idempotent():
     p1 = _capi.ensure_built()
     mtime = os.path.getmtime(p1)
