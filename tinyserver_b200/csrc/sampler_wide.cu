@@ -266,24 +266,33 @@ __device__ __forceinline__ uint32_t valid2(int cnt, int q) {
     return (2 * q < cnt ? 0x0000ffffu : 0u) | (2 * q + 1 < cnt ? 0xffff0000u : 0u);
 }
 
+// One group's elements maximised pairwise: both halves of the result hold
+// candidates for the group's largest x (missing elements read as -inf).
+template <typename T>
+__device__ __forceinline__ uint32_t group_max2(const Raw8<T>& g) {
+    uint32_t m = hmax2u<T>(hmax2u<T>(g.v[0].x, g.v[0].y), hmax2u<T>(g.v[0].z, g.v[0].w));
+    if (g.cnt < 8) {  // the tail: only the elements that exist
+        m = ninf2<T>();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t ok = valid2(g.cnt, q);
+            m = hmax2u<T>(m, (word(g.v[0], q) & ok) | (ninf2<T>() & ~ok));
+        }
+    }
+    return m;
+}
+
+template <typename T>
+__device__ __forceinline__ float max_of2(uint32_t m) {
+    return fmaxf(f_of_bits16<T>(m & 0xffffu), f_of_bits16<T>(m >> 16));
+}
+
 template <typename T, int L>
 __device__ __forceinline__ float groups_max(const Raw8<T> (&r)[L]) {
     uint32_t v = ninf2<T>();
 #pragma unroll
-    for (int u = 0; u < L; ++u) {
-        uint32_t m = hmax2u<T>(hmax2u<T>(r[u].v[0].x, r[u].v[0].y),
-                               hmax2u<T>(r[u].v[0].z, r[u].v[0].w));
-        if (r[u].cnt < 8) {  // the tail: only the elements that exist
-            m = ninf2<T>();
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const uint32_t ok = valid2(r[u].cnt, q);
-                m = hmax2u<T>(m, (word(r[u].v[0], q) & ok) | (ninf2<T>() & ~ok));
-            }
-        }
-        v = hmax2u<T>(v, m);
-    }
-    return fmaxf(f_of_bits16<T>(v & 0xffffu), f_of_bits16<T>(v >> 16));
+    for (int u = 0; u < L; ++u) v = hmax2u<T>(v, group_max2<T>(r[u]));
+    return max_of2<T>(v);
 }
 
 // The (row, chunk) of this CTA in the row passes: its first element and count.
@@ -332,19 +341,33 @@ __global__ void __launch_bounds__(kWThreads) wide_max_kernel(const WideDev a) {
             // the groups' largest x by packed maxima; only when it beats the
             // running best, the first element holding it (equal x, +0 and
             // -0 included, give equal s)
-            const float gm = groups_max<T, kLoads>(r);
+            float gmu[kLoads];
+            float gm = -INFINITY;
+#pragma unroll
+            for (int u = 0; u < kLoads; ++u) {
+                gmu[u] = max_of2<T>(group_max2<T>(r[u]));
+                gm = fmaxf(gm, gmu[u]);
+            }
             const bool any = r[0].cnt > 0;  // group 0 holds this thread's first elements
             if (any && (best_i == kNone || gm > best)) {
-                bool found = false;
+                // the first group holding gm, then its first element holding it
+                // (descending loops: the last match written is the first one)
+                int uu = 0;
+                uint4 v = r[0].v[0];
 #pragma unroll
-                for (int u = 0; u < kLoads; ++u)
+                for (int u = kLoads - 1; u >= 0; --u)
+                    if (gmu[u] == gm) {
+                        uu = u;
+                        v = r[u].v[0];
+                    }
+                int jj = -1;  // stays -1 only when no element compares equal (NaN)
 #pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        if (!found && j < r[u].cnt && x_at<T>(r[u], j) == gm) {
-                            found = true;
-                            best = gm;
-                            best_i = 8u * (uint32_t)(g0 + u * kWThreads + threadIdx.x) + j;
-                        }
+                for (int j = 7; j >= 0; --j)
+                    if (f_of_bits16<T>((word(v, j >> 1) >> (16 * (j & 1))) & 0xffffu) == gm) jj = j;
+                if (jj >= 0) {
+                    best = gm;
+                    best_i = 8u * (uint32_t)(g0 + uu * kWThreads + threadIdx.x) + jj;
+                }
             }
         } else {
 #pragma unroll
@@ -796,6 +819,7 @@ __global__ void __launch_bounds__(kWThreads) wide_compact_kernel(const WideDev a
             fetch_any<T>(p, n, g0, a.vec, r);
             take = body(r);
         }
+        if (!__any_sync(0xffffffffu, take != 0)) continue;  // the usual case: nothing here
         const uint32_t mine = __popcll(take);
         uint32_t incl = mine;
 #pragma unroll
