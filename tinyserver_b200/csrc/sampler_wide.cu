@@ -253,6 +253,24 @@ __device__ __forceinline__ uint32_t hmax2u(uint32_t a, uint32_t b) {
         asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
     return d;
 }
+// Packed a >= b and a <= b of two 16-bit values: 0xffff per true half
+// (false for NaN).
+template <typename T>
+__device__ __forceinline__ uint32_t ge2(uint32_t a, uint32_t b) {
+    if constexpr (std::is_same<T, __half>::value)
+        return __hge2_mask(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+    else
+        return __hge2_mask(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                           *reinterpret_cast<const __nv_bfloat162*>(&b));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t le2(uint32_t a, uint32_t b) {
+    if constexpr (std::is_same<T, __half>::value)
+        return __hle2_mask(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+    else
+        return __hle2_mask(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                           *reinterpret_cast<const __nv_bfloat162*>(&b));
+}
 template <typename T>
 __device__ __forceinline__ uint32_t ninf2() {
     return std::is_same<T, __half>::value ? 0xfc00fc00u : 0xff80ff80u;
@@ -773,9 +791,19 @@ __global__ void __launch_bounds__(kWThreads) wide_compact_kernel(const WideDev a
     const int r1_lo = (int)h.r1_lo, r1_hi = (int)h.r1_hi, r2_lo = (int)h.r2_lo,
               r2_hi = (int)h.r2_hi;
     const uint32_t k1lo = h.k1_lo, k1hi = h.k1_hi, k2lo = h.k2_lo, k2hi = h.k2_hi;
-    // every candidate's x is at least that of the lowest taken key
+    // the key ranges as value bounds, both halves (an empty range's bounds are
+    // NaN, which no value compares to); every candidate's x is at least that
+    // of the lowest taken key
     float xlow = 0.0f;
-    if constexpr (kRaw) xlow = x_of_key16<T>(k2lo <= k2hi ? min(k1lo, k2lo) : k1lo);
+    uint32_t lo1 = 0, hi1 = 0, lo2 = 0, hi2 = 0;
+    if constexpr (kRaw) {
+        const uint32_t kp = key16_of_float<T>(INFINITY);
+        lo1 = bits_of_key16(k1lo) * 0x00010001u;
+        hi1 = bits_of_key16(min(k1hi, kp)) * 0x00010001u;
+        lo2 = k2lo <= k2hi ? bits_of_key16(k2lo) * 0x00010001u : ninf2<T>() | 0x00400040u;
+        hi2 = k2lo <= k2hi ? bits_of_key16(min(k2hi, kp)) * 0x00010001u : lo2;
+        xlow = x_of_key16<T>(k2lo <= k2hi ? min(k1lo, k2lo) : k1lo);
+    }
     const T* p = reinterpret_cast<const T*>(a.logits) + row * a.row_stride + lo;
     u64* cand = a.cand + row * kCandCap;
     const int ng = (n + 7) / 8;
@@ -790,12 +818,14 @@ __global__ void __launch_bounds__(kWThreads) wide_compact_kernel(const WideDev a
 #pragma unroll
         for (int u = 0; u < kLoads; ++u) {
             if constexpr (kRaw) {
-                if (look) {
+                if (look) {  // packed value compares against the ranges' bounds
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const uint32_t kx = key16_of_bits(bits16<T>(r[u], j));
-                        if (j < r[u].cnt && ((kx >= k1lo && kx <= k1hi) || (kx >= k2lo && kx <= k2hi)))
-                            take |= 1ull << (8 * u + j);
+                    for (int q = 0; q < 4; ++q) {
+                        const uint32_t w = word(r[u].v[0], q);
+                        const uint32_t t = ((ge2<T>(w, lo1) & le2<T>(w, hi1)) |
+                                            (ge2<T>(w, lo2) & le2<T>(w, hi2))) &
+                                           valid2(r[u].cnt, q);
+                        take |= (u64)((t & 1u) | ((t >> 15) & 2u)) << (8 * u + 2 * q);
                     }
                 }
             } else {
