@@ -319,10 +319,10 @@ inline int check_launch() {
 // Launch a kernel that calls pdl_wait() before touching global memory, with
 // programmatic stream serialization (see pdl_wait).
 template <typename... KArgs, typename... Args>
-int launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem,
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, unsigned block, size_t smem,
                cudaStream_t stream, Args... args) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
+    cfg.gridDim = grid;
     cfg.blockDim = dim3(block);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;

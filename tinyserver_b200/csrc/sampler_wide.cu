@@ -331,6 +331,8 @@ __device__ __forceinline__ float row_max_s(u64 maxkey, float tc) {
 // ---- P1 --------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(kWThreads) wide_max_kernel(const WideDev a) {
+    pdl_wait();  // the previous pass's writes are visible from here
+    pdl_trigger();
     const int64_t row = blockIdx.y;
     int64_t lo;
     const int n = chunk_elems(a, lo);
@@ -445,6 +447,8 @@ __global__ void __launch_bounds__(kWThreads) wide_max_kernel(const WideDev a) {
 // ---- P2 --------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(kWThreads) wide_hist_kernel(const WideDev a) {
+    pdl_wait();  // the previous pass's writes are visible from here
+    pdl_trigger();
     constexpr bool kRaw = sizeof(T) == 2;
     constexpr int kCntBins = kRaw ? kRawBins : kDepthBins;
     const int64_t row = blockIdx.y;
@@ -620,6 +624,8 @@ __device__ uint32_t lowest_key16(uint32_t lo, uint32_t hi, P&& pred) {
 
 template <typename T>
 __global__ void __launch_bounds__(kSThreads) wide_bounds_kernel(const WideDev a) {
+    pdl_wait();  // the previous pass's writes are visible from here
+    pdl_trigger();
     constexpr bool kRaw = sizeof(T) == 2;
     const int64_t row = blockIdx.x;
     RowHdr& h = a.hdr[row];
@@ -780,6 +786,8 @@ __global__ void __launch_bounds__(kSThreads) wide_bounds_kernel(const WideDev a)
 // ---- P4 --------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(kWThreads) wide_compact_kernel(const WideDev a) {
+    pdl_wait();  // the previous pass's writes are visible from here
+    pdl_trigger();
     constexpr bool kRaw = sizeof(T) == 2;
     const int64_t row = blockIdx.y;
     RowHdr& h = a.hdr[row];
@@ -936,6 +944,8 @@ __device__ __forceinline__ float s_of_cand(u64 key) { return key_value(~(uint32_
 constexpr size_t kSelSmem = 3 * (size_t)kCandCap * sizeof(u64) + kDepthBins * sizeof(u64);
 
 __global__ void __launch_bounds__(kPThreads) wide_select_kernel(const WideDev a) {
+    pdl_wait();  // the previous pass's writes are visible from here
+    pdl_trigger();
     extern __shared__ __align__(16) u64 wsm[];
     u64* grouped = wsm;                 // candidate keys grouped by bin
     u64* w = wsm + kCandCap;            // inclusive masses in the grouped order
@@ -1142,13 +1152,18 @@ int launch_wide(const WideDev& d, int64_t B, int nchunk, cudaStream_t stream) {
         if (e != cudaSuccess) return launch_failed(e);
         sized.fetch_or(bit, std::memory_order_relaxed);
     }
+    // the passes after the first start with programmatic dependent launch:
+    // each one's launch and prologue overlap the previous pass's tail, and it
+    // waits for that pass (pdl_wait) before its first global access
     const dim3 rows_grid((unsigned)nchunk, (unsigned)B);
     wide_max_kernel<T><<<rows_grid, kWThreads, 0, stream>>>(d);
-    wide_hist_kernel<T><<<rows_grid, kWThreads, 0, stream>>>(d);
-    wide_bounds_kernel<T><<<(unsigned)B, kSThreads, 0, stream>>>(d);
-    wide_compact_kernel<T><<<rows_grid, kWThreads, 0, stream>>>(d);
-    wide_select_kernel<<<(unsigned)B, kPThreads, kSelSmem, stream>>>(d);
-    return check_launch();
+    int rc = check_launch();
+    if (rc == QF_OK) rc = launch_pdl(wide_hist_kernel<T>, rows_grid, kWThreads, 0, stream, d);
+    if (rc == QF_OK) rc = launch_pdl(wide_bounds_kernel<T>, dim3((unsigned)B), kSThreads, 0, stream, d);
+    if (rc == QF_OK) rc = launch_pdl(wide_compact_kernel<T>, rows_grid, kWThreads, 0, stream, d);
+    if (rc == QF_OK)
+        rc = launch_pdl(wide_select_kernel, dim3((unsigned)B), kPThreads, kSelSmem, stream, d);
+    return rc;
 }
 
 }  // namespace
