@@ -575,15 +575,17 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     # every two kernels (on the launch stream); these events serialise the
     # launches, so this pass runs a little slower than the headline pass.
     nk = len(Step.KERNELS)
-    kb = min(args.steps, 200)
+    kb = max(50, min(args.steps, 200))
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)] for _ in range(kb)]
+    for _ in range(3):
+        step.run(t)
     torch.cuda.synchronize()
     for i in range(kb):
         step.run(t, evs[i])
     torch.cuda.synchronize()
-    per_kernel_us = {}
+    per_kernel_us = {}  # the median over the steps: one disturbed step does not move it
     for j, name in enumerate(Step.KERNELS):
-        per_kernel_us[name] = 1e3 * sum(e[j].elapsed_time(e[j + 1]) for e in evs) / kb
+        per_kernel_us[name] = 1e3 * statistics.median(e[j].elapsed_time(e[j + 1]) for e in evs)
     tsb.check_errors(dev)
 
     # ---- each kernel alone: a 256 MB read between launches evicts L2, so every
@@ -658,8 +660,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "hbm_peak_kind": peak_kind,
         "kernels": kernels,
         "kernels_note": "per-kernel CUDA-event times from a second pass with an event between "
-                        f"every two launches ({kb} steps, {attributed_ms:.4f} ms per step); "
-                        "the headline is the pass without them",
+                        f"every two launches (median over {kb} steps; the medians sum to "
+                        f"{attributed_ms:.4f} ms); the headline is the pass without them",
         "kernels_isolated": kernels_isolated,
         "kernels_isolated_note": "each kernel alone on the step's inputs, median of 20 launches, "
                                  "a 256 MB read between launches so its inputs come from HBM; "
