@@ -684,6 +684,7 @@ __global__ void __launch_bounds__(kSThreads) wide_bounds_kernel(const WideDev a)
         if constexpr (kRaw) {
             // raw bins from the top: position q is bin kRawBins - 1 - q (staged
             // through shared memory so the global reads are coalesced)
+#pragma unroll 8
             for (int b = threadIdx.x; b < kRawBins; b += kSThreads) stage[b] = a.cnt[row * kRawBins + b];
             __syncthreads();
             u64 w[kRawPer];
@@ -710,6 +711,7 @@ __global__ void __launch_bounds__(kSThreads) wide_bounds_kernel(const WideDev a)
         }
     } else {
         u64* stage64 = reinterpret_cast<u64*>(stage);
+#pragma unroll 8
         for (int b = threadIdx.x; b < kDepthBins; b += kSThreads)
             stage64[b] = a.mas[row * kDepthBins + b];
         __syncthreads();
@@ -970,9 +972,22 @@ __global__ void __launch_bounds__(kPThreads) wide_select_kernel(const WideDev a)
         return min(nb - 1, max(0, depth_bin(s_of_cand(key), m) - d_lo));
     };
     // ---- counting sort by bin ----------------------------------------------
+    // a thread's candidates, all loaded at once and kept for the scatter
+    constexpr int kPer = kCandCap / kPThreads;
+    u64 ck[kPer];
+    int cb[kPer];
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+        const int i = (int)threadIdx.x + q * kPThreads;
+        ck[q] = i < n ? cand[i] : 0;
+    }
     for (int b = threadIdx.x; b <= nb; b += kPThreads) sh.cnt[b] = 0;
     __syncthreads();
-    for (int i = threadIdx.x; i < n; i += kPThreads) atomicAdd(&sh.cnt[bin_of(cand[i])], 1u);
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+        cb[q] = bin_of(ck[q]);
+        if ((int)threadIdx.x + q * kPThreads < n) atomicAdd(&sh.cnt[cb[q]], 1u);
+    }
     __syncthreads();
     for (int b = threadIdx.x; b < nb; b += kPThreads) bbase[b] = sh.cnt[b];
     __syncthreads();
@@ -983,11 +998,10 @@ __global__ void __launch_bounds__(kPThreads) wide_select_kernel(const WideDev a)
     }
     if (threadIdx.x == 0) sh.off[nb] = (uint32_t)n;
     __syncthreads();
-    for (int i = threadIdx.x; i < n; i += kPThreads) {
-        const u64 key = cand[i];
-        const int b = bin_of(key);
-        grouped[sh.off[b] + atomicAdd(&sh.cnt[b], 1u)] = key;
-    }
+#pragma unroll
+    for (int q = 0; q < kPer; ++q)
+        if ((int)threadIdx.x + q * kPThreads < n)
+            grouped[sh.off[cb[q]] + atomicAdd(&sh.cnt[cb[q]], 1u)] = ck[q];
     __syncthreads();
     for (int i = threadIdx.x; i < n; i += kPThreads) w[i] = mass_of(s_of_cand(grouped[i]), m);
     __syncthreads();
