@@ -1494,7 +1494,7 @@ def run_sample(args, rank: int, world: int, local_rank: int, as_row: bool = Fals
                    "rows": B, "vocab": V, "l2": "3 rotating logits buffers (233 MB > L2)"},
         "roofline": roofline("hbm", "batch-wide sampler (5 kernels + cluster kernel for the rows "
                              "it leaves)" if path == "wide" else "sample_kernel", gbs, "GB/s",
-                             None if path == "wide" else ncu_traffic("sample_kernel"),
+                             ncu_traffic("sampler_batch_wide" if path == "wide" else "sample_kernel"),
                              bytes_per_launch=nbytes),
         "path": {"taken": path, "ms_per_step": {path: round(per_ms, 4),
                                                 other: round(other_ms, 4)},
