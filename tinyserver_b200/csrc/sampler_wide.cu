@@ -36,14 +36,15 @@
 // 16 <= d < 144, the rest in the last bin.  The bin is non-decreasing in d,
 // so the elements at or above a bin are a head of the rank order, and equal s
 // share a bin.  For 16-bit logits the max, the top-k counts and the
-// compaction work on the logits' own 16-bit order keys, two per 32-bit word,
-// without the division: for distinct 16-bit values x < x', x / t and x' / t
-// differ by at least 2^-11 relative, far above float32 rounding, so the order
-// of s is the order of x wherever s is a finite normal number.  P3 checks
-// that at the maximum and at every key threshold it sets (the values on
-// either side must give different s) and sends the row to the cluster kernel
-// otherwise.  Top-k rows of 16-bit logits count by the top 13 bits of the
-// 16-bit key.  fp32 logits divide in every pass.
+// compaction work on the logits themselves, two per 32-bit word (packed
+// bf16x2 / f16x2 maxima and compares, 16-bit order keys), without the
+// division: for distinct 16-bit values x < x', x / t and x' / t differ by at
+// least 2^-11 relative, far above float32 rounding, so the order of s is the
+// order of x wherever s is a finite normal number.  P3 checks that at the
+// maximum and at every key threshold it sets (the values on either side must
+// give different s) and sends the row to the cluster kernel otherwise.  Top-k
+// rows of 16-bit logits count by the top 13 bits of the 16-bit key, in the 24
+// such bins below the maximum's.  fp32 logits divide in every pass.
 #include <cfloat>
 
 #include "qf_sample.cuh"
