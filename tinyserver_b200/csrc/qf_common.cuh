@@ -280,9 +280,11 @@ __device__ __forceinline__ void flag(int32_t* status, int32_t bits) {
 // with programmatic stream serialization: the next kernel in the stream may be
 // launched -- its CTAs scheduled onto SMs as the previous kernel's retire --
 // before the previous one has finished.  Every kernel launched that way calls
-// pdl_wait() before its first global memory access, which blocks until the
-// preceding grid has completed and its writes are visible, so the overlap is
-// only launch latency and CTA rasterisation, never data.  pdl_trigger()
+// pdl_wait() before its first access to memory that earlier work in the
+// stream may still write, which blocks until the preceding grid has completed
+// and its writes are visible, so the overlap is only launch latency, CTA
+// rasterisation and loads of inputs known to be final, never data that is in
+// flight.  pdl_trigger()
 // allows the following grid to begin launching.
 #ifndef QF_PDL
 #define QF_PDL 1

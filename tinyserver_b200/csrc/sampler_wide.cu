@@ -551,8 +551,17 @@ __global__ void __launch_bounds__(kWThreads) wide_hist_kernel(const WideDev a) {
 
 // ---- P3 --------------------------------------------------------------------
 constexpr int kSThreads = 256;
+constexpr int kSWarps = kSThreads / 32;
 constexpr int kDepthPer = kDepthBins / kSThreads;  // depth bins per thread
 constexpr int kRawPer = kRawBins / kSThreads;      // raw bins per thread
+// The row's histogram is staged in shared memory with one pad word after
+// every 32 raw bins (one pad u64 after every 16 depth bins), so that the
+// threads' reads of their runs of consecutive bins fall into distinct banks.
+__device__ __forceinline__ int raw_slot(int b) { return b + (b >> 5); }
+__device__ __forceinline__ int depth_slot(int b) { return b + (b >> 4); }
+constexpr int kStageWords = kRawBins + kRawBins / 32;
+static_assert(2 * (kDepthBins + kDepthBins / 16) <= kStageWords, "depth staging fits");
+constexpr int kCrossSlots = 3;  // crossings one P3 CTA takes
 
 struct Cross {
     uint32_t pos;  // kNone: not reached
@@ -560,14 +569,16 @@ struct Cross {
     u64 through;   // and through it
 };
 
-// Over positions 0 .. PER * kSThreads - 1 (thread t holds [PER t, PER t + PER)
-// in w): the first position whose weight is > 0 and whose inclusive
-// cumulative weight reaches tau.  Whole CTA.
+struct CrossShared {
+    u64 wsum[kSWarps];
+    uint32_t first[kCrossSlots];
+    u64 before[kCrossSlots], through[kCrossSlots];
+};
+
+// Thread t holds positions [PER t, PER t + PER) in w: the total weight of
+// every position before its first.  Whole CTA, once per CTA.
 template <int PER>
-__device__ Cross block_crossing(const u64 (&w)[PER], u64 tau) {
-    __shared__ u64 s_wsum[kSThreads / 32];
-    __shared__ uint32_t s_first;
-    __shared__ u64 s_before, s_through;
+__device__ u64 block_before(const u64 (&w)[PER], CrossShared& sh) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     u64 sum = 0;
 #pragma unroll
@@ -578,71 +589,241 @@ __device__ Cross block_crossing(const u64 (&w)[PER], u64 tau) {
         const u64 x = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += x;
     }
-    __syncthreads();  // earlier readers of the shared results are done
-    if (lane == 31) s_wsum[warp] = incl;
-    if (threadIdx.x == 0) s_first = kNone;
+    if (lane == 31) sh.wsum[warp] = incl;
     __syncthreads();
     u64 before = incl - sum;
-    for (int q = 0; q < warp; ++q) before += s_wsum[q];
-    uint32_t mine = kNone;
-    u64 mb = 0, mt = 0, cum = before;
+#pragma unroll
+    for (int q = 0; q < kSWarps; ++q) before += q < warp ? sh.wsum[q] : 0;
+    return before;
+}
+
+// NC crossings at once, into shared slots [slot, slot + NC) that no earlier
+// call used (their `first` set to kNone before the CTA's first barrier): for
+// each tau, the first position whose weight is > 0 and whose inclusive
+// cumulative weight reaches tau.  `before` from block_before.  Whole CTA.
+template <int PER, int NC>
+__device__ void block_cross(const u64 (&w)[PER], u64 before, const u64 (&tau)[NC], int slot,
+                            CrossShared& sh, Cross (&c)[NC]) {
+    uint32_t mine[NC];
+    u64 mb[NC], mt[NC];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+        mine[k] = kNone;
+        mb[k] = mt[k] = 0;
+    }
+    u64 cum = before;
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
         const u64 prev = cum;
         cum += w[i];
-        if (mine == kNone && w[i] > 0 && cum >= tau) {
-            mine = (uint32_t)(PER * threadIdx.x + i);
-            mb = prev;
-            mt = cum;
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            if (mine[k] == kNone && w[i] > 0 && cum >= tau[k]) {
+                mine[k] = (uint32_t)(PER * threadIdx.x + i);
+                mb[k] = prev;
+                mt[k] = cum;
+            }
         }
     }
-    if (mine != kNone) atomicMin(&s_first, mine);
-    __syncthreads();
-    const uint32_t first = s_first;
-    if (mine != kNone && mine == first) {
-        s_before = mb;
-        s_through = mt;
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+        const uint32_t wmin = __reduce_min_sync(0xffffffffu, mine[k]);
+        if ((threadIdx.x & 31) == 0 && wmin != kNone) atomicMin(&sh.first[slot + k], wmin);
     }
     __syncthreads();
-    Cross c;
-    c.pos = first;
-    c.before = first == kNone ? 0 : s_before;
-    c.through = first == kNone ? 0 : s_through;
-    return c;
+    uint32_t first[NC];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+        first[k] = sh.first[slot + k];
+        if (mine[k] != kNone && mine[k] == first[k]) {
+            sh.before[slot + k] = mb[k];
+            sh.through[slot + k] = mt[k];
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+        c[k].pos = first[k];
+        c[k].before = first[k] == kNone ? 0 : sh.before[slot + k];
+        c[k].through = first[k] == kNone ? 0 : sh.through[slot + k];
+    }
 }
 
-// Smallest 16-bit key k in [lo, hi] with pred(k), given pred(hi) and pred
-// monotone (false, then true).
-template <typename P>
-__device__ uint32_t lowest_key16(uint32_t lo, uint32_t hi, P&& pred) {
-    while (lo < hi) {
-        const uint32_t mid = (lo + hi) >> 1;
-        if (pred(mid)) hi = mid;
-        else lo = mid + 1;
+// For each of NS depth bins D: the smallest 16-bit key in [kninf, kpinf]
+// whose s lands in a bin <= D (kpinf + 1 when D < 0).  s(+inf) is in bin 0
+// and the bin does not increase with the key, so each search is for the
+// first true value of a monotone predicate that holds at kpinf.  `clean` is
+// cleared when a found key's s equals the s of the key below it.  Whole CTA;
+// D uniform; `ks` zeroed (nfalse, bad) before the CTA's first barrier.
+//
+// A window of kKeyWin keys around the key where s = m - (the lower edge of
+// bin D + 1) is tested with one key per thread, and two more threads test
+// the key below the window (must be false) and the one above it (must be
+// true).  When both hold, the count of false tests is the answer's offset,
+// and the s values the threads found answer the `clean` check.  A search
+// whose window misses (not met with finite rows) takes the whole key range
+// in rounds: each splits the keys below the upper end into kSThreads runs,
+// one thread tests the last key of each, and the count of false tests gives
+// the run holding the first true key (65,536 keys: two rounds).
+constexpr int kKeyWin = kSThreads - 2;
+constexpr int kKeySearches = 4;
+
+struct KeyShared {
+    float s[kKeySearches][kSThreads];
+    uint32_t nfalse[kKeySearches];
+    uint32_t bad;
+};
+
+template <typename T, int NS>
+__device__ void block_key_thresholds(const int (&D)[NS], float tc, float m, uint32_t kninf,
+                                     uint32_t kpinf, uint32_t (&t)[NS], bool& clean,
+                                     KeyShared& ks) {
+    static_assert(NS <= kKeySearches, "key-search slots");
+    auto s_of = [&](uint32_t q) { return scaled<float>(x_of_key16<T>(q), tc); };
+    const int tid = (int)threadIdx.x, lane = tid & 31;
+    uint32_t wlo[NS];
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+        t[s] = kpinf + 1;
+        wlo[s] = kninf;
+        if (D[s] < 0) continue;
+        const int e = D[s] + 1;
+        const float edge = e <= 1024 ? (float)e * (1.0f / 64.0f) : 16.0f + (float)(e - 1024) * 0.125f;
+        const uint32_t kc = key16_of_float<T>((m - edge) * tc);
+        uint32_t w0 = kc > kninf + kKeyWin / 2 ? kc - kKeyWin / 2 : kninf;
+        if (w0 > kpinf - kKeyWin) w0 = kpinf - kKeyWin;
+        wlo[s] = w0;
+        // thread i < kKeyWin tests w0 + i, thread kKeyWin the key below the
+        // window, thread kKeyWin + 1 the window's top w0 + kKeyWin
+        const bool none = tid == kKeyWin && w0 == kninf;  // no key below
+        const uint32_t q = tid < kKeyWin ? w0 + tid : (tid == kKeyWin ? w0 - 1 : w0 + kKeyWin);
+        float sv = 0.0f;
+        bool p = false;
+        if (!none) {
+            sv = s_of(q);
+            p = depth_bin(sv, m) <= D[s];
+        }
+        ks.s[s][tid] = sv;
+        const bool f = tid < kKeyWin && !p;
+        const bool bad = (tid == kKeyWin && p) || (tid == kKeyWin + 1 && !p);
+        const uint32_t nf = (uint32_t)__popc(__ballot_sync(0xffffffffu, f));
+        const bool anybad = __any_sync(0xffffffffu, bad);
+        if (lane == 0) {
+            if (nf) atomicAdd(&ks.nfalse[s], nf);
+            if (anybad) atomicOr(&ks.bad, 1u << s);
+        }
     }
-    return lo;
+    __syncthreads();
+    const uint32_t bad = ks.bad;
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+        if (D[s] < 0 || ((bad >> s) & 1u)) continue;
+        const uint32_t nf = ks.nfalse[s];
+        t[s] = wlo[s] + nf;
+        if (t[s] > kninf) {  // s at the found key and at the key below it
+            const float s_at = ks.s[s][nf < (uint32_t)kKeyWin ? (int)nf : kKeyWin + 1];
+            const float s_below = ks.s[s][nf > 0 ? (int)nf - 1 : kKeyWin];
+            clean = clean && s_below != s_at;
+        }
+    }
+    if (bad == 0) return;
+    uint32_t lo[NS], hi[NS];
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+        lo[s] = kninf;
+        hi[s] = D[s] >= 0 && ((bad >> s) & 1u) ? kpinf : kninf;
+    }
+    for (int round = 0; round < 4; ++round) {  // two rounds for 16-bit keys, a third finds nothing left
+        uint32_t step[NS];
+        bool f[NS];
+        bool any = false;
+#pragma unroll
+        for (int s = 0; s < NS; ++s) {
+            const uint32_t n = hi[s] - lo[s];
+            step[s] = (n + kSThreads - 1) / kSThreads;
+            const uint32_t q = lo[s] + (threadIdx.x + 1) * step[s] - 1;
+            f[s] = n > 0 && q < hi[s] && depth_bin(s_of(q), m) > D[s];
+            any = any || n > 0;
+        }
+        if (!any) break;
+#pragma unroll
+        for (int s = 0; s < NS; ++s) {
+            const uint32_t nf = (uint32_t)__syncthreads_count(f[s]);
+            if (hi[s] > lo[s]) {
+                lo[s] += nf * step[s];
+                hi[s] = min(hi[s], lo[s] + step[s] - 1);
+            }
+        }
+    }
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+        if (D[s] < 0 || !((bad >> s) & 1u)) continue;
+        t[s] = lo[s];
+        clean = clean && (lo[s] <= kninf || s_of(lo[s] - 1) != s_of(lo[s]));
+    }
 }
+
+// Top-k rows of 16-bit logits: over the row's top PER x kSThreads raw bins
+// (position q is bin kRawBins - 1 - q), the first position whose cumulative
+// count reaches k_eff.  Whole CTA.
+template <int PER>
+__device__ Cross raw_crossing(const uint32_t* cnt_row, u64 k_eff, uint32_t* stage, CrossShared& xs) {
+    constexpr int kPos = PER * kSThreads;
+    constexpr int kVec = kPos / 4 / kSThreads;
+    static_assert(kPos % (4 * kSThreads) == 0 && kPos <= kRawBins, "whole 16-byte loads");
+    const uint4* src = reinterpret_cast<const uint4*>(cnt_row + (kRawBins - kPos));
+    uint4 v[kVec];
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) v[i] = src[threadIdx.x + i * kSThreads];
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) {
+        const int b = 4 * ((int)threadIdx.x + i * kSThreads);  // from bin kRawBins - kPos
+        stage[raw_slot(b)] = v[i].x;
+        stage[raw_slot(b + 1)] = v[i].y;
+        stage[raw_slot(b + 2)] = v[i].z;
+        stage[raw_slot(b + 3)] = v[i].w;
+    }
+    __syncthreads();
+    u64 w[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) w[i] = stage[raw_slot(kPos - 1 - (PER * (int)threadIdx.x + i))];
+    const u64 before = block_before<PER>(w, xs);
+    const u64 tau[1] = {k_eff};
+    Cross c[1];
+    block_cross<PER, 1>(w, before, tau, 0, xs, c);
+    return c[0];
+}
+constexpr int kRawTop = 2048;  // the short scan's bins
 
 template <typename T>
 __global__ void __launch_bounds__(kSThreads) wide_bounds_kernel(const WideDev a) {
-    pdl_wait();  // the previous pass's writes are visible from here
-    pdl_trigger();
     constexpr bool kRaw = sizeof(T) == 2;
     const int64_t row = blockIdx.x;
+    // The row's settings are inputs that no pass writes, and all the work
+    // queued before P1 has completed by the time this grid launches (P1 is
+    // launched without overlap, and P2's CTAs release this grid only after
+    // their own wait on P1), so they load while the wait below runs.
+    const float temp = a.temperature[row];
+    const int64_t k = row_top_k(a, row);
+    const float top_p = a.top_p[row];
+    const float u = a.uniforms ? a.uniforms[row]
+                               : uniform_from_hash((uint64_t)a.seeds[row], (uint64_t)a.steps[row]);
+    pdl_wait();  // the previous pass's writes are visible from here
+    pdl_trigger();
     RowHdr& h = a.hdr[row];
     const u64 maxkey = h.maxkey;
+    const u64 z_all = h.z_all;
     const uint32_t argmax = ~(uint32_t)maxkey;
-    const float temp = a.temperature[row];
     const float tc = fmaxf(temp, 1e-5f);
     const float m = row_max_s<T>(maxkey, tc);
     // 16-bit logits: the order of s must be the order of x at the maximum --
     // a finite normal s, and the next lower 16-bit value giving a lower s
     bool plain = true;
-    uint32_t kninf = 0, kpinf = 0;
+    uint32_t kninf = 0, kpinf = 0, k16 = 0;  // k16: the maximum's 16-bit key
     if constexpr (kRaw) {
         kninf = key16_of_float<T>(-INFINITY);
         kpinf = key16_of_float<T>(INFINITY);
-        const uint32_t k16 = key16_of_float<T>(key_value((uint32_t)(maxkey >> 32)));
+        k16 = key16_of_float<T>(key_value((uint32_t)(maxkey >> 32)));
         plain = isfinite(m) && fabsf(m) >= FLT_MIN && k16 > kninf && k16 <= kpinf &&
                 scaled<float>(x_of_key16<T>(k16 - 1), tc) != m;
     }
@@ -659,42 +840,32 @@ __global__ void __launch_bounds__(kSThreads) wide_bounds_kernel(const WideDev a)
         return;
     }
     const int64_t V = a.vocab;
-    const int64_t k = row_top_k(a, row);
     const u64 k_eff = (k > 0 && k < V) ? (u64)k : (u64)V;
-    const float top_p = a.top_p[row];
-    const float u = a.uniforms ? a.uniforms[row]
-                               : uniform_from_hash((uint64_t)a.seeds[row], (uint64_t)a.steps[row]);
     const bool use_k = k_eff < (u64)V, use_p = top_p < 1.0f;
-    __shared__ __align__(16) uint32_t stage[kRawBins];  // the row's histogram
+    __shared__ __align__(16) uint32_t stage[kStageWords];  // the row's histogram, padded
+    __shared__ CrossShared xs;
+    __shared__ KeyShared ks;
+    if (threadIdx.x < kCrossSlots) xs.first[threadIdx.x] = kNone;
+    if (threadIdx.x < kKeySearches) ks.nfalse[threadIdx.x] = 0;
+    if (threadIdx.x == 0) ks.bad = 0;
     // depth-bin ranges [r1_lo, r1_hi] and [r2_lo, r2_hi] (empty: lo > hi)
     uint32_t r1_lo = 0, r1_hi = 0, r2_lo = 1, r2_hi = 0;
     u64 base_mas = 0;
     bool ok = true;
     uint32_t k1_lo = 1, k1_hi = 0, k2_lo = 1, k2_hi = 0;  // 16-bit key ranges (inclusive)
-    // the smallest key whose bin is <= D, when s differs on either side of it
-    auto key_thr = [&](int D, bool& clean) -> uint32_t {
-        if (D < 0) return kpinf + 1;
-        const uint32_t t = lowest_key16(kninf, kpinf, [&](uint32_t q) {
-            return depth_bin(scaled<float>(x_of_key16<T>(q), tc), m) <= D;
-        });
-        clean = clean && (t <= kninf || scaled<float>(x_of_key16<T>(t - 1), tc) !=
-                                            scaled<float>(x_of_key16<T>(t), tc));
-        return t;
-    };
     if (use_k) {
         if constexpr (kRaw) {
-            // raw bins from the top: position q is bin kRawBins - 1 - q (staged
-            // through shared memory so the global reads are coalesced)
-#pragma unroll 8
-            for (int b = threadIdx.x; b < kRawBins; b += kSThreads) stage[b] = a.cnt[row * kRawBins + b];
-            __syncthreads();
-            u64 w[kRawPer];
-#pragma unroll
-            for (int i = 0; i < kRawPer; ++i)
-                w[i] = stage[kRawBins - 1 - (kRawPer * (int)threadIdx.x + i)];
-            const Cross c = block_crossing<kRawPer>(w, k_eff);
-            const uint32_t t16 = c.pos == kNone ? 0 : (uint32_t)(kRawBins - 1 - c.pos) << 3;
-            ok = c.pos != kNone && c.through <= (u64)kCandCap && t16 > kninf && t16 <= kpinf &&
+            // P2 counted only the bins from kRawWindow below the maximum's up;
+            // when those are all among the top kRawTop, only those are read
+            const uint32_t bmin = (k16 >> 3) > kRawWindow ? (k16 >> 3) - kRawWindow : 0u;
+            const uint32_t* cnt_row = a.cnt + row * kRawBins;
+            Cross c[1];
+            if (bmin >= (uint32_t)(kRawBins - kRawTop))
+                c[0] = raw_crossing<kRawTop / kSThreads>(cnt_row, k_eff, stage, xs);
+            else
+                c[0] = raw_crossing<kRawPer>(cnt_row, k_eff, stage, xs);
+            const uint32_t t16 = c[0].pos == kNone ? 0 : (uint32_t)(kRawBins - 1 - c[0].pos) << 3;
+            ok = c[0].pos != kNone && c[0].through <= (u64)kCandCap && t16 > kninf && t16 <= kpinf &&
                  scaled<float>(x_of_key16<T>(t16 - 1), tc) != scaled<float>(x_of_key16<T>(t16), tc);
             if (ok) {
                 k1_lo = t16;
@@ -706,60 +877,80 @@ __global__ void __launch_bounds__(kSThreads) wide_bounds_kernel(const WideDev a)
 #pragma unroll
             for (int i = 0; i < kDepthPer; ++i)
                 w[i] = a.cnt[row * kRawBins + kDepthPer * threadIdx.x + i];
-            const Cross c = block_crossing<kDepthPer>(w, k_eff);
-            ok = c.pos != kNone && c.through <= (u64)kCandCap;
-            r1_hi = c.pos;
+            const u64 before = block_before<kDepthPer>(w, xs);
+            const u64 tau[1] = {k_eff};
+            Cross c[1];
+            block_cross<kDepthPer, 1>(w, before, tau, 0, xs, c);
+            ok = c[0].pos != kNone && c[0].through <= (u64)kCandCap;
+            r1_hi = c[0].pos;
         }
     } else {
         u64* stage64 = reinterpret_cast<u64*>(stage);
-#pragma unroll 8
-        for (int b = threadIdx.x; b < kDepthBins; b += kSThreads)
-            stage64[b] = a.mas[row * kDepthBins + b];
+        const uint4* src = reinterpret_cast<const uint4*>(a.mas + row * kDepthBins);
+        constexpr int kVec = kDepthBins / 2 / kSThreads;
+        uint4 v[kVec];
+#pragma unroll
+        for (int i = 0; i < kVec; ++i) v[i] = src[threadIdx.x + i * kSThreads];
+#pragma unroll
+        for (int i = 0; i < kVec; ++i) {
+            const int b = 2 * ((int)threadIdx.x + i * kSThreads);
+            stage64[depth_slot(b)] = ((u64)v[i].y << 32) | v[i].x;
+            stage64[depth_slot(b + 1)] = ((u64)v[i].w << 32) | v[i].z;
+        }
         __syncthreads();
         u64 w[kDepthPer];
 #pragma unroll
-        for (int i = 0; i < kDepthPer; ++i) w[i] = stage64[kDepthPer * threadIdx.x + i];
-        const u64 z_all = h.z_all;
-        u64 tau;
+        for (int i = 0; i < kDepthPer; ++i) w[i] = stage64[depth_slot(kDepthPer * (int)threadIdx.x + i)];
+        const u64 before = block_before<kDepthPer>(w, xs);
+        u64 tau[1];
         if (use_p) {
             const double theta = (double)top_p * (double)z_all;
-            tau = theta < 0.0 ? 0 : (u64)floor(theta) + 1;
+            tau[0] = theta < 0.0 ? 0 : (u64)floor(theta) + 1;
         } else {
-            tau = (u64)ceil((double)u * (double)z_all);
-            if (tau > z_all) tau = z_all;
+            tau[0] = (u64)ceil((double)u * (double)z_all);
+            if (tau[0] > z_all) tau[0] = z_all;
         }
-        const Cross c = block_crossing<kDepthPer>(w, tau);
-        ok = c.pos != kNone;
-        r1_lo = r1_hi = c.pos;
-        base_mas = c.before;
+        Cross c[1];
+        block_cross<kDepthPer, 1>(w, before, tau, 0, xs, c);
+        ok = c[0].pos != kNone;
+        r1_lo = r1_hi = c[0].pos;
+        base_mas = c[0].before;
         if (ok && use_p) {
             // the kept mass lies within the cut bin's cumulative bounds, so
             // the pick's threshold u * (kept mass) lies within u times them
-            u64 t_lo = (u64)ceil((double)u * (double)c.before);
-            if (t_lo > c.before) t_lo = c.before;
-            u64 t_hi = (u64)ceil((double)u * (double)c.through);
-            if (t_hi > c.through) t_hi = c.through;
-            const Cross cl = block_crossing<kDepthPer>(w, t_lo);
-            const Cross ch = block_crossing<kDepthPer>(w, t_hi);
-            ok = cl.pos != kNone && ch.pos != kNone && cl.pos <= ch.pos && ch.pos <= c.pos;
+            u64 t2[2];
+            t2[0] = (u64)ceil((double)u * (double)c[0].before);
+            if (t2[0] > c[0].before) t2[0] = c[0].before;
+            t2[1] = (u64)ceil((double)u * (double)c[0].through);
+            if (t2[1] > c[0].through) t2[1] = c[0].through;
+            Cross cl[2];
+            block_cross<kDepthPer, 2>(w, before, t2, 1, xs, cl);
+            ok = cl[0].pos != kNone && cl[1].pos != kNone && cl[0].pos <= cl[1].pos &&
+                 cl[1].pos <= c[0].pos;
             if (ok) {
-                if (ch.pos + 1 >= c.pos) {
-                    r1_lo = cl.pos;
+                if (cl[1].pos + 1 >= c[0].pos) {
+                    r1_lo = cl[0].pos;
                 } else {
-                    r2_lo = r2_hi = c.pos;
-                    r1_lo = cl.pos;
-                    r1_hi = ch.pos;
+                    r2_lo = r2_hi = c[0].pos;
+                    r1_lo = cl[0].pos;
+                    r1_hi = cl[1].pos;
                 }
-                base_mas = cl.before;
+                base_mas = cl[0].before;
             }
         }
         if constexpr (kRaw) {
             if (ok) {
-                k1_lo = key_thr((int)r1_hi, ok);
-                k1_hi = key_thr((int)r1_lo - 1, ok) - 1;
-                if (r2_lo <= r2_hi) {
-                    k2_lo = key_thr((int)r2_hi, ok);
-                    k2_hi = key_thr((int)r2_lo - 1, ok) - 1;
+                // the smallest key whose bin is <= each range's ends
+                const bool two = r2_lo <= r2_hi;
+                const int D[4] = {(int)r1_hi, (int)r1_lo - 1, two ? (int)r2_hi : -1,
+                                  two ? (int)r2_lo - 1 : -1};
+                uint32_t t[4];
+                block_key_thresholds<T, 4>(D, tc, m, kninf, kpinf, t, ok, ks);
+                k1_lo = t[0];
+                k1_hi = t[1] - 1;
+                if (two) {
+                    k2_lo = t[2];
+                    k2_hi = t[3] - 1;
                 }
             }
         }
@@ -972,6 +1163,15 @@ __global__ void __launch_bounds__(kPThreads) wide_select_kernel(const WideDev a)
     auto bin_of = [&](u64 key) {
         return min(nb - 1, max(0, depth_bin(s_of_cand(key), m) - d_lo));
     };
+    // a row without top-k: its histogram's masses of bins d_lo on, loaded now
+    // and used once the candidates are grouped
+    constexpr int kBinPer = kDepthBins / kPThreads;
+    u64 hm[kBinPer];
+#pragma unroll
+    for (int q = 0; q < kBinPer; ++q) {
+        const int b = (int)threadIdx.x + q * kPThreads;
+        hm[q] = !use_k && b < nb ? a.mas[row * kDepthBins + d_lo + b] : 0;
+    }
     // ---- counting sort by bin ----------------------------------------------
     // a thread's candidates, all loaded at once and kept for the scatter
     constexpr int kPer = kCandCap / kPThreads;
@@ -1016,12 +1216,18 @@ __global__ void __launch_bounds__(kPThreads) wide_select_kernel(const WideDev a)
     } else {
         // the histogram's bin masses from d_lo on, summed onto the mass
         // ranked above d_lo: scratch[b] is the mass through bin b
-        for (int b = threadIdx.x; b < nb; b += kPThreads)
-            scratch[b] = a.mas[row * kDepthBins + d_lo + b];
+#pragma unroll
+        for (int q = 0; q < kBinPer; ++q) {
+            const int b = (int)threadIdx.x + q * kPThreads;
+            if (b < nb) scratch[b] = hm[q];
+        }
         __syncthreads();
         block_scan_u64(scratch, nb, h.base_mas, sh);
-        for (int b = threadIdx.x; b < nb; b += kPThreads)
-            bbase[b] = scratch[b] - a.mas[row * kDepthBins + d_lo + b];
+#pragma unroll
+        for (int q = 0; q < kBinPer; ++q) {
+            const int b = (int)threadIdx.x + q * kPThreads;
+            if (b < nb) bbase[b] = scratch[b] - hm[q];
+        }
         __syncthreads();
         // rebase w: the grouped prefix at each bin's start, replaced by bbase
         for (int b = threadIdx.x; b < nb; b += kPThreads)
