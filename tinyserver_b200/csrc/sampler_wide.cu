@@ -61,6 +61,9 @@ namespace {
 #ifndef QF_WIDE_CAND
 #define QF_WIDE_CAND 2048  // candidates a row may have on this path
 #endif
+#ifndef QF_WIDE_SEL_THREADS
+#define QF_WIDE_SEL_THREADS 256  // threads of a P5 CTA (one row)
+#endif
 
 constexpr int kWThreads = 512;
 constexpr int kWWarps = kWThreads / 32;
@@ -1088,8 +1091,10 @@ __global__ void __launch_bounds__(kWThreads) wide_compact_kernel(const WideDev a
 }
 
 // ---- P5 --------------------------------------------------------------------
-constexpr int kPThreads = 256;
+constexpr int kPThreads = QF_WIDE_SEL_THREADS;
 constexpr int kPWarps = kPThreads / 32;
+static_assert(kPWarps <= 32 && kCandCap % kPThreads == 0 && kDepthBins % kPThreads == 0,
+              "select: one scan warp, whole per-thread shares");
 
 struct SelShared {
     uint32_t cnt[kDepthBins + 1];  // candidates per bin (relative to d_lo)
